@@ -1,0 +1,355 @@
+"""Benchmark of the quantized forward path (one JSON line on rank 0).
+
+Default workload (the configuration the headline metric is quoted on): the
+Qwen2.5-0.5B architecture, random-init N(0, 0.02), INT8 per-channel weights,
+fp32 activations; batch 1; a 512-token random prompt chunk-prefilled in
+128-token chunks, then 50 greedy decode tokens; KV block size 16.
+
+One step = one such request end to end (prefill + 50 tokens).  The metric is
+generated tokens per second per GPU, with the prefill inside the timed
+region as in the reference's own tok/s figure (new tokens / generate time);
+the decode-only rate is reported beside it.  Multi-GPU: the model shards
+nowhere at this size, so each rank runs an independent replica (weak
+scaling) and ``value`` sums the ranks' tokens over the slowest rank's time.
+
+``--impl reference`` times the CPU oracle (a restatement of the reference's
+own algorithm, see oracle/) on this box's host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    "qwen05b-int8": dict(preset="qwen2.5-0.5b", quantize="int8", prompt=512, chunk=128, new=50,
+                         block=16),
+    "qwen05b-int4": dict(preset="qwen2.5-0.5b", quantize="int4", prompt=512, chunk=128, new=50,
+                         block=16),
+    "tiny-int8": dict(preset="tiny-llama", quantize="int8", prompt=32, chunk=16, new=16, block=16),
+}
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d.get("bf16_tflops"), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def run_ours(args, wl):
+    from kshipra_b200.config import PRESETS
+    from kshipra_b200.model import KshipraModel, DecodeState
+    from kshipra_b200.weights import synthetic_state_dict
+    import kshipra_b200._lib as L
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+    cfg = PRESETS[wl["preset"]]
+    sd = synthetic_state_dict(cfg, seed=0, device=dev)
+    km = KshipraModel(config=cfg, state_dict=sd, quantize=wl["quantize"], device=dev)
+    del sd
+    torch.cuda.empty_cache()
+    P, C, NEW, B = wl["prompt"], wl["chunk"], wl["new"], wl["block"]
+    g = torch.Generator().manual_seed(rank)
+    prompt = torch.randint(0, cfg.vocab, (P,), generator=g).tolist()
+    nb = (P + NEW + B - 1) // B
+    alloc = km.new_pool(nb, B)
+    bt = list(range(nb))
+
+    # One decode state reused by every step: the graph is captured once.
+    st = DecodeState(km, alloc.pool, [bt], NEW)
+
+    def device_step():
+        first = km.prefill(prompt, alloc.pool, bt, C)
+        st.start(first.view(1), [P])
+        st.step_eager() if st.graph is None else st.graph.replay()
+        for _ in range(NEW - 2):
+            st.graph.replay()
+
+    # warm-up (captures the graph)
+    first = km.prefill(prompt, alloc.pool, bt, C)
+    st.start(first.view(1), [P])
+    st.step_eager()
+    st.capture()
+    for _ in range(max(args.warmup, 3)):
+        device_step()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            device_step()
+        e1.record(stream)
+        barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    tokens = st.history[0, :NEW].cpu().tolist()
+
+    # decode-only rate: graph replays alone
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    first = km.prefill(prompt, alloc.pool, bt, C)
+    st.start(first.view(1), [P])
+    torch.cuda.synchronize()
+    d0.record(stream)
+    for _ in range(NEW - 1):
+        st.graph.replay()
+    d1.record(stream)
+    torch.cuda.synchronize()
+    decode_ms_per_tok = d0.elapsed_time(d1) / (NEW - 1)
+
+    # end to end through the public API: host prompt list in, host token list out
+    h2d = P * 8
+    d2h = NEW * 8
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    a0.record(stream)
+    for _ in range(args.steps):
+        out = km.generate(prompt, max_new_tokens=NEW, block_size=B, prefill_chunk=C)
+    a1.record(stream)
+    barrier()
+    e2e_ms = a0.elapsed_time(a1) / args.steps
+    assert out == tokens, "public API and device loop disagree"
+
+    # dominant kernel: the fp32 lm_head GEMV + argmax, timed alone
+    hbm, _, peak_kind = measured_peaks()
+    x = torch.randn((1, cfg.hidden), device=dev)
+    tok = torch.empty(1, dtype=torch.int64, device=dev)
+    lm_ws = torch.zeros(int(L.lib().ksh_lm_head_workspace_size(1, cfg.vocab)), dtype=torch.uint8,
+                        device=dev)
+    for _ in range(5):
+        km._lm_head_argmax(x, tok, ws=lm_ws)
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    R = 50
+    r0.record(stream)
+    for _ in range(R):
+        km._lm_head_argmax(x, tok, ws=lm_ws)
+    r1.record(stream)
+    torch.cuda.synchronize()
+    lm_ms = r0.elapsed_time(r1) / R
+    lm_bytes = cfg.vocab * cfg.hidden * 4 + cfg.hidden * 4
+    achieved = lm_bytes / (lm_ms * 1e-3) / 1e9
+
+    # max over ranks
+    t = torch.tensor([ms, e2e_ms, decode_ms_per_tok], dtype=torch.float64, device=dev)
+    if ws > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms, e2e_ms, decode_ms_per_tok = t.tolist()
+    wb = km.weight_bytes()
+    res = dict(
+        metric="decode tok/s/GPU (generated tokens / request time incl. 512-token chunked prefill)",
+        value=ws * NEW / (ms * 1e-3), unit="tok/s", n_gpus=ws, steps=args.steps,
+        warmup=max(args.warmup, 3), ms_per_step=ms, higher_is_better=True, scaling="weak",
+        vs_baseline=None, dtype="fp32 act / " + wl["quantize"] + " weights", data="synthetic",
+        config={"workload": args.workload, "model": cfg.name, "quantize": wl["quantize"],
+                "global_batch": ws, "prompt_len": P, "prefill_chunk": C, "new_tokens": NEW,
+                "block_size": B, "parallelism": f"replicas x{ws}",
+                "l2": "inputs larger than L2 (weights streamed per token: "
+                      f"{(wb['layers'] + wb['lm_head']) / 1e6:.0f} MB)"},
+        decode_only={"value": ws * 1e3 / decode_ms_per_tok, "unit": "tok/s",
+                     "ms_per_token": decode_ms_per_tok,
+                     "bytes_per_token": wb["layers"] + wb["lm_head"],
+                     "hbm_frac_of_" + peak_kind: (wb["layers"] + wb["lm_head"]) /
+                     (decode_ms_per_tok * 1e-3) / 1e9 / hbm},
+        e2e={"value": ws * NEW / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+             "d2h_bytes_per_step": d2h},
+        roofline={"kernel": "lm_head fp32 GEMV + argmax (ksh_lm_head_argmax)", "bound": "hbm",
+                  "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                  "peak_kind": peak_kind, "traffic": None,
+                  "algorithmic_bytes_per_launch": lm_bytes, "launch_ms": lm_ms},
+        gpu_launches=None,
+        clocks=clk.summary(),
+    )
+    n_layers = cfg.layers
+    per_tok = n_layers * 8 + 1 + 2 + 1
+    per_chunk = n_layers * 8 + 2 + 1
+    res["gpu_launches"] = args.steps * ((P + C - 1) // C * per_chunk + 1 + (NEW - 1) * per_tok)
+    if rank == 0 and not args.no_cpu_baseline and ws == 1:
+        res["cpu_baseline"] = cpu_baseline(wl, cfg, prompt, samples=1)
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+    return res, rank
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle (reference algorithm) timing
+# ---------------------------------------------------------------------------
+
+def cpu_baseline(wl, cfg, prompt, samples=1):
+    """Bounded sample of the workload on the CPU oracle: the full chunked
+    prefill plus 2 decode tokens, extrapolated to the workload's tok/s."""
+    from oracle.model import OracleModel
+    from kshipra_b200.weights import synthetic_state_dict
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sd = synthetic_state_dict(cfg, seed=0)
+    om = OracleModel(cfg, sd, wl["quantize"])
+    P, C, NEW, B = wl["prompt"], wl["chunk"], wl["new"], wl["block"]
+    tp, td = [], []
+    for _ in range(samples):
+        nb = (P + NEW + B - 1) // B
+        pool = om.new_pool(nb, B)
+        bt = list(range(nb))
+        t0 = time.perf_counter()
+        pos = 0
+        while pos < P:
+            c = min(C, P - pos)
+            ids = torch.tensor([prompt[pos:pos + c]])
+            om.forward(ids, torch.arange(pos, pos + c).unsqueeze(0), pool, bt,
+                       [bt[p // B] * B + p % B for p in range(pos, pos + c)], prefix_len=pos)
+            pos += c
+        tp.append(time.perf_counter() - t0)
+        for s in range(2):
+            p = P + s
+            t0 = time.perf_counter()
+            om.forward(torch.tensor([[1]]), torch.tensor([[p]]), pool, bt,
+                       [bt[p // B] * B + p % B], prefix_len=p)
+            td.append(time.perf_counter() - t0)
+    t_pref = statistics.mean(tp)
+    t_dec = statistics.mean(td)
+    value = NEW / (t_pref + NEW * t_dec)
+    return {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"oracle.model on {threads} threads: {samples}x full {P}-token prefill "
+                      f"({t_pref:.2f}s) + 2 decode tokens ({t_dec:.2f}s/token), "
+                      f"extrapolated to {NEW} tokens",
+            "prefill_s": t_pref, "decode_s_per_token": t_dec}
+
+
+def run_reference(args, wl):
+    ws, rank, local = dist_env()
+    if rank != 0:
+        return None, rank
+    from kshipra_b200.config import PRESETS
+    cfg = PRESETS[wl["preset"]]
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab, (wl["prompt"],), generator=g).tolist()
+    cb = cpu_baseline(wl, cfg, prompt, samples=max(1, min(args.steps, 2)))
+    res = dict(metric="decode tok/s/GPU (generated tokens / request time incl. 512-token chunked prefill)",
+               value=cb["value"], unit="tok/s", n_gpus=ws, steps=args.steps,
+               warmup=args.warmup, ms_per_step=1e3 * wl["new"] / cb["value"],
+               higher_is_better=True, scaling="weak", vs_baseline=None,
+               dtype="fp32 act / " + wl["quantize"] + " weights", data="synthetic",
+               config={"workload": args.workload, "model": cfg.name, "quantize": wl["quantize"],
+                       "global_batch": 1, "prompt_len": wl["prompt"],
+                       "prefill_chunk": wl["chunk"], "new_tokens": wl["new"],
+                       "block_size": wl["block"], "parallelism": "cpu"},
+               impl="reference", cpu_baseline=cb,
+               e2e={"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0})
+    return res, rank
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="qwen05b-int8", choices=sorted(WORKLOADS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        res, rank = run_reference(args, wl)
+    else:
+        res, rank = run_ours(args, wl)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,184 @@
+/*
+ * kshipra_b200 -- C ABI of the B200 (sm_100a) quantized forward path.
+ *
+ * Every entry point takes raw device pointers, int64 sizes and a CUDA stream
+ * (passed as void*, a cudaStream_t), launches asynchronously on that stream
+ * and returns an int status (KSH_OK = 0, negative on a host-side argument
+ * error or a failed launch).  Nothing here allocates: the caller owns every
+ * buffer, including the workspaces whose sizes the *_workspace_size helpers
+ * report.  Data-dependent errors found on the device (bad block id, slot,
+ * position, token id, non-finite weight) are OR-ed into a caller-owned int32
+ * status word as KSH_FLAG_* bits; kernels never trap.
+ *
+ * Functions are stateless and may be called from any host thread; calls on
+ * one stream are ordered, calls on different streams that share a workspace
+ * race.
+ *
+ * Each declaration names the reference interface it replaces
+ * (Hedau0404/Kshipra, path:line).
+ */
+#ifndef KSHIPRA_B200_H
+#define KSHIPRA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (return values) ---- */
+#define KSH_OK               0
+#define KSH_ERR_SHAPE       -1   /* bad size / shape argument */
+#define KSH_ERR_ALIGN       -2   /* pointer not aligned as required */
+#define KSH_ERR_CUDA        -3   /* launch failed; see ksh_last_cuda_error() */
+#define KSH_ERR_UNSUPPORTED -4   /* shape outside what the kernels handle */
+#define KSH_ERR_WORKSPACE   -5   /* workspace missing or too small */
+
+/* ---- device status-word bits ---- */
+#define KSH_FLAG_NONFINITE     1   /* weight holds NaN/Inf (QuantizationError) */
+#define KSH_FLAG_BAD_BLOCK     2   /* block-table entry outside [0, num_blocks) */
+#define KSH_FLAG_BAD_SLOT      4   /* slot outside the pool */
+#define KSH_FLAG_BAD_POSITION  8   /* position outside the RoPE table */
+#define KSH_FLAG_BAD_TOKEN    16   /* token id outside [0, vocab) */
+#define KSH_FLAG_BAD_LENGTH   32   /* sequence longer than its block table */
+
+int ksh_abi_version(void);
+const char* ksh_status_string(int status);
+/* cudaError_t recorded by the last call that returned KSH_ERR_CUDA. */
+int ksh_last_cuda_error(void);
+/* Enable (1) / disable (0) programmatic dependent launch; returns previous. */
+int ksh_set_pdl(int enabled);
+
+/* ------------------------------------------------------------------------
+ * Weight packing.  w: fp32 [n, k] row-major.
+ * ---------------------------------------------------------------------- */
+
+/* Replaces quantize_int8_per_channel, engine/quantization.py:196-223.
+ * payload int8 [n, k]; scales fp16 bits [n]. */
+int ksh_pack_int8(const float* w, int64_t n, int64_t k, int8_t* payload,
+                  uint16_t* scales, int32_t* flags, void* stream);
+
+/* Replaces quantize_int4_per_group, engine/quantization.py:238-318.
+ * group_size even and > 0; k_padded = ceil(k / g) * g;
+ * payload uint8 [n, k_padded / 2] (low nibble = even k);
+ * scales fp16 bits [n, k_padded / g]. */
+int ksh_pack_int4(const float* w, int64_t n, int64_t k, int64_t group_size,
+                  uint8_t* payload, uint16_t* scales, int32_t* flags, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Linear layers (replace QuantizedLinear.forward, engine/quantization.py:
+ * 394-396, and nn.Linear for unquantized weights):
+ *   y[m, j] = sum_k x[m, k] * W[j, k] + bias[j] + residual[m, j]
+ * x fp32 [m, k]; bias [n] or NULL; residual [m, n] or NULL (may alias y).
+ * M <= 16 runs the decode GEMV; larger M the tensor-core GEMM, which needs
+ * the workspace reported by ksh_linear_workspace_size (else NULL/0).
+ * ---------------------------------------------------------------------- */
+int64_t ksh_linear_workspace_size(int64_t m, int64_t k, int64_t n);
+
+int ksh_qlinear_w8(const float* x, int64_t m, int64_t k, const int8_t* payload,
+                   const uint16_t* scales, const float* bias, const float* residual,
+                   float* y, int64_t n, void* workspace, int64_t workspace_bytes,
+                   void* stream);
+
+int ksh_qlinear_w4(const float* x, int64_t m, int64_t k, const uint8_t* payload,
+                   const uint16_t* scales, int64_t group_size, int64_t k_padded,
+                   const float* bias, const float* residual, float* y, int64_t n,
+                   void* workspace, int64_t workspace_bytes, void* stream);
+
+int ksh_linear_f32(const float* x, int64_t m, int64_t k, const float* w,
+                   const float* bias, const float* residual, float* y, int64_t n,
+                   void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Gate/up projection fused with SwiGLU (replaces LlamaMLP's
+ * act(gate_proj(x)) * up_proj(x), called at engine/model.py:147):
+ * the weight holds 2*inter rows, gate rows [0, inter) then up rows
+ * [inter, 2*inter); h[m, j] = silu(g[m, j]) * u[m, j]. */
+int ksh_qlinear_swiglu_w8(const float* x, int64_t m, int64_t k, const int8_t* payload,
+                          const uint16_t* scales, float* h, int64_t inter,
+                          void* workspace, int64_t workspace_bytes, void* stream);
+int ksh_qlinear_swiglu_w4(const float* x, int64_t m, int64_t k, const uint8_t* payload,
+                          const uint16_t* scales, int64_t group_size, int64_t k_padded,
+                          float* h, int64_t inter, void* workspace,
+                          int64_t workspace_bytes, void* stream);
+int ksh_linear_swiglu_f32(const float* x, int64_t m, int64_t k, const float* w,
+                          float* h, int64_t inter, void* workspace,
+                          int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Embedding + RMSNorm (HF Embedding / LlamaRMSNorm, engine/model.py:107,113,
+ * 146,150).  rmsnorm: y = w * (x * rsqrt(mean(x^2) + eps)), fp32.
+ * ---------------------------------------------------------------------- */
+int ksh_embedding(const int64_t* ids, int64_t m, const float* table, int64_t vocab,
+                  int64_t hidden, float* out, int32_t* flags, void* stream);
+int ksh_rmsnorm(const float* x, const float* w, float* y, int64_t m, int64_t hidden,
+                float eps, void* stream);
+
+/* ------------------------------------------------------------------------
+ * RoPE at absolute positions + K/V scatter into the block pool
+ * (replaces _apply_rope + the per-token pool write, engine/model.py:108,121,
+ * 123-129).  qkv fp32 [m, (hq + 2*hkv) * d] (q heads, then k, then v);
+ * rope_cos / rope_sin fp32 [max_pos, d/2] (cos/sin of position * inv_freq);
+ * q_out fp32 [m, hq, d]; pool fp32 [num_blocks, num_layers, 2, hkv,
+ * block_size, d]; slot = block_id * block_size + offset.
+ * ---------------------------------------------------------------------- */
+int ksh_rope_kv_write(const float* qkv, int64_t m, int64_t hq, int64_t hkv, int64_t d,
+                      const int64_t* positions, const int64_t* slot_mapping,
+                      const float* rope_cos, const float* rope_sin, int64_t max_pos,
+                      float* q_out, float* pool, int64_t num_blocks, int64_t num_layers,
+                      int64_t layer, int64_t block_size, int32_t* flags, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Paged online-softmax attention over the block pool (replaces
+ * chunked_attention, engine/chunked_prefill.py:93-140), batched over
+ * sequences (varlen).  Sequence s owns query rows [q_start[s], q_start[s+1])
+ * of q [T, hq, d], at absolute positions prefix_lens[s] + i; it attends to
+ * keys 0 .. prefix_lens[s] + len - 1 stored through
+ * block_tables[s * max_blocks + j] with a causal mask.  GQA: query head h
+ * reads kv head h / (hq / hkv).  q_start / prefix_lens live on the device
+ * (they may change between graph replays); max_q_len and max_total_len are
+ * host-side upper bounds used to size the grid.
+ * ---------------------------------------------------------------------- */
+int64_t ksh_paged_attention_workspace_size(int64_t num_seqs, int64_t hq, int64_t hkv,
+                                           int64_t d, int64_t max_q_len,
+                                           int64_t max_total_len);
+int ksh_paged_attention(const float* q, int64_t hq, int64_t d, const float* pool,
+                        int64_t num_blocks, int64_t num_layers, int64_t layer,
+                        int64_t hkv, int64_t block_size, const int32_t* block_tables,
+                        int64_t max_blocks, const int32_t* q_start,
+                        const int32_t* prefix_lens, int64_t num_seqs, int64_t max_q_len,
+                        int64_t max_total_len, float* out, void* workspace,
+                        int64_t workspace_bytes, int32_t* flags, void* stream);
+
+/* ------------------------------------------------------------------------
+ * lm_head (fp32, never quantized; engine/model.py:151) fused with the greedy
+ * argmax of generate (model.py:187, 200; first index of the maximum, as
+ * torch.argmax).  logits [m, vocab] may be NULL (argmax only).
+ * ---------------------------------------------------------------------- */
+int64_t ksh_lm_head_workspace_size(int64_t m, int64_t vocab);
+int ksh_lm_head_argmax(const float* x, int64_t m, int64_t hidden, const float* w,
+                       int64_t vocab, float* logits, int64_t* tokens, void* workspace,
+                       int64_t workspace_bytes, void* stream);
+/* Row-wise argmax of materialised logits [m, vocab]. */
+int ksh_argmax_rows(const float* logits, int64_t m, int64_t vocab, int64_t* out,
+                    void* stream);
+
+/* ------------------------------------------------------------------------
+ * Greedy decode bookkeeping on the device, so a decode step can be replayed
+ * from a CUDA graph without a host round trip (replaces the host side of
+ * generate's loop, engine/model.py:194-203).  For each sequence b:
+ *   ids[b] = next[b]; history[b * hist_stride + step[0]] = next[b];
+ *   positions[b] += 1; prefix_lens[b] = positions[b];
+ *   slots[b] = block_tables[b * max_blocks + pos / B] * B + pos % B
+ * and step[0] += 1 (once).
+ * ---------------------------------------------------------------------- */
+int ksh_decode_advance(const int64_t* next, int64_t batch, int64_t* ids,
+                       int64_t* positions, int32_t* prefix_lens, int64_t* slots,
+                       const int32_t* block_tables, int64_t max_blocks,
+                       int64_t block_size, int64_t* history, int64_t hist_stride,
+                       int64_t* step, int32_t* flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KSHIPRA_B200_H */

@@ -1,0 +1,83 @@
+// Host-side runtime helpers: device properties, launch options, status text.
+
+#include <stdlib.h>
+#include <string.h>
+
+#include <atomic>
+#include <mutex>
+#include <unordered_map>
+#include <utility>
+
+#include "common.cuh"
+
+namespace ksh {
+
+namespace {
+std::atomic<int> g_last_cuda_error{0};
+
+int env_flag(const char* name, int dflt) {
+  const char* v = getenv(name);
+  if (!v || !*v) return dflt;
+  return atoi(v) != 0;
+}
+std::atomic<int> g_pdl{env_flag("KSH_PDL", 1)};
+std::atomic<int> g_prefetch{env_flag("KSH_L2_PREFETCH", 1)};
+}  // namespace
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
+bool prefetch_enabled() { return g_prefetch.load(std::memory_order_relaxed) != 0; }
+
+int record_cuda_error(cudaError_t e) {
+  g_last_cuda_error.store(static_cast<int>(e));
+  return KSH_ERR_CUDA;
+}
+
+int num_sms() {
+  static std::mutex mu;
+  static std::unordered_map<int, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  int n = 148;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  cache[dev] = n;
+  return n;
+}
+
+int set_smem_optin(const void* kernel, size_t bytes) {
+  // cudaFuncSetAttribute is per device; cache (device, kernel) -> bytes set.
+  static std::mutex mu;
+  static std::unordered_map<const void*, std::unordered_map<int, size_t>> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  size_t& cur = done[kernel][dev];
+  if (cur >= bytes) return KSH_OK;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(bytes));
+  if (e != cudaSuccess) return record_cuda_error(e);
+  cur = bytes;
+  return KSH_OK;
+}
+
+}  // namespace ksh
+
+extern "C" int ksh_abi_version(void) { return 1; }
+
+extern "C" int ksh_last_cuda_error(void) { return ksh::g_last_cuda_error.load(); }
+
+extern "C" int ksh_set_pdl(int enabled) { return ksh::g_pdl.exchange(enabled ? 1 : 0); }
+
+extern "C" const char* ksh_status_string(int status) {
+  switch (status) {
+    case KSH_OK: return "ok";
+    case KSH_ERR_SHAPE: return "invalid shape or size argument";
+    case KSH_ERR_ALIGN: return "pointer not aligned as required";
+    case KSH_ERR_CUDA: return "CUDA launch failed";
+    case KSH_ERR_UNSUPPORTED: return "shape not supported by the kernels";
+    case KSH_ERR_WORKSPACE: return "workspace missing or too small";
+    default: return "unknown status";
+  }
+}

@@ -1,0 +1,451 @@
+"""KshipraModel on the B200: the quantized forward through the CUDA kernels.
+
+Drop-in for the reference's engine/model.py ``KshipraModel``:
+
+* ``KshipraModel(hf_model, device, quantize)`` (model.py:61-91) takes a HF
+  Llama / Qwen2 ``*ForCausalLM`` and quantizes all seven projections per
+  layer (INT8 per channel or INT4 per group of 128; ``None`` keeps fp32);
+  embeddings and ``lm_head`` stay fp32;
+* ``forward(input_ids, position_ids, pool, block_table, slot_mapping,
+  prefix_len)`` (model.py:93-151) returns logits ``[1, L, vocab]`` and writes
+  the chunk's K/V into ``pool`` (BlockAllocator layout);
+* ``generate(prompt_ids, max_new_tokens, eos_token_id, block_size)``
+  (model.py:154-205) is greedy decoding with a fresh pool.
+
+Per layer the forward runs: RMSNorm -> fused q/k/v dequant-linear (+bias) ->
+RoPE + K/V scatter into the pool -> paged attention -> o_proj with the
+residual add fused -> RMSNorm -> fused gate/up dequant-linear with SwiGLU ->
+down_proj with the residual add fused.  The decode step of ``generate``
+(embedding -> layers -> final norm -> lm_head + argmax -> on-device position /
+slot advance) is captured once in a CUDA graph and replayed per token, so
+greedy decoding has no host round trip until the end.
+
+Weights for q/k/v and gate/up are packed into one buffer each (per-row
+quantization makes that byte-identical to packing them separately); the
+per-projection ``QuantizedLinear`` modules exposed on ``layers[i]`` are views
+into those buffers.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import call, ptr, stream_ptr
+from .chunked_prefill import AttentionWorkspace, paged_attention
+from .config import ModelConfig
+from .prefix_cache import BlockAllocator
+from .quantization import (QuantizedLinear, QuantizedWeight, Workspace, linear_launch,
+                           quantize_int4_per_group, quantize_int8_per_channel, swiglu_launch)
+
+FLAG_NAMES = {1: "non-finite weight", 2: "block id out of range", 4: "slot out of range",
+              8: "position outside the RoPE table", 16: "token id out of range",
+              32: "sequence longer than its block table"}
+
+
+class KshipraDeviceError(IndexError):
+    """A kernel reported a data-dependent error through the device status word."""
+
+
+def _check_flags(flags: torch.Tensor) -> None:
+    f = int(flags.item())
+    if f:
+        names = [n for b, n in FLAG_NAMES.items() if f & b]
+        flags.zero_()
+        raise KshipraDeviceError("device reported: " + ", ".join(names))
+
+
+def rope_tables(head_dim: int, theta: float, max_pos: int):
+    """cos / sin of position * inv_freq, [max_pos, head_dim/2], by the
+    reference's formula (model.py:35-44) evaluated on the CPU in fp32."""
+    inv_freq = 1.0 / (theta ** (torch.arange(0, head_dim, 2).float() / head_dim))
+    pos = torch.arange(max_pos).float()
+    freqs = torch.einsum("i,j->ij", pos, inv_freq)
+    return freqs.cos().contiguous(), freqs.sin().contiguous()
+
+
+@dataclass
+class _Proj:
+    """One (possibly fused) projection: quantized or fp32."""
+    qw: Optional[QuantizedWeight]
+    w: Optional[torch.Tensor]
+    bias: Optional[torch.Tensor]
+    n: int
+
+
+class _Layer:
+    pass
+
+
+class KshipraModel:
+    """Runs a Llama / Qwen2 model through the B200 kernels."""
+
+    def __init__(self, hf_model=None, device: torch.device = None, quantize: Optional[str] = None,
+                 *, config: Optional[ModelConfig] = None,
+                 state_dict: Optional[Dict[str, torch.Tensor]] = None, group_size: int = 128) -> None:
+        if quantize not in (None, "int8", "int4"):
+            raise ValueError(f"quantize must be None, 'int8' or 'int4', got {quantize!r}")
+        if device is None or torch.device(device).type != "cuda":
+            if not torch.cuda.is_available():
+                raise _lib.KshipraLibraryError("KshipraModel runs on CUDA only (no CPU path)")
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(device)
+        if self.device.index is None:
+            self.device = torch.device("cuda", torch.cuda.current_device())
+        if hf_model is not None:
+            config = ModelConfig.from_hf_config(hf_model.config)
+            state_dict = hf_model.state_dict()
+        if config is None or state_dict is None:
+            raise ValueError("pass an HF model, or config= and state_dict=")
+        _lib.lib()
+        self.model = hf_model
+        self.cfg = config
+        self.quantize = quantize
+        self.group_size = group_size
+        self.n_heads = config.heads
+        self.n_kv_heads = config.kv_heads
+        self.head_dim = config.head_dim
+        self.n_layers = config.layers
+        self.vocab_size = config.vocab
+        self.hidden = config.hidden
+        self.inter = config.intermediate
+        self.eps = float(config.rms_eps)
+        self._rope_theta = float(config.rope_theta)
+        self._rope = None
+        self.max_positions = config.max_positions
+        self.flags = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._lin_ws = Workspace()
+        self._attn_ws = AttentionWorkspace()
+        self._lm_ws: Optional[torch.Tensor] = None
+        with torch.cuda.device(self.device):
+            self._load(state_dict)
+
+    # ------------------------------------------------------------------ #
+    # weights
+    # ------------------------------------------------------------------ #
+
+    def _pack(self, w: torch.Tensor) -> _Proj:
+        if self.quantize == "int8":
+            return _Proj(quantize_int8_per_channel(w), None, None, w.shape[0])
+        if self.quantize == "int4":
+            return _Proj(quantize_int4_per_group(w, self.group_size), None, None, w.shape[0])
+        return _Proj(None, w.to(self.device, torch.float32).contiguous(), None, w.shape[0])
+
+    def _view(self, proj: _Proj, r0: int, r1: int, bias=None):
+        """QuantizedLinear / fp32 weight view of rows [r0, r1) of a fused projection."""
+        if proj.qw is None:
+            lin = torch.nn.Linear(proj.w.shape[1], r1 - r0, bias=bias is not None,
+                                  device="meta")
+            lin.weight = torch.nn.Parameter(proj.w[r0:r1], requires_grad=False)
+            if bias is not None:
+                lin.bias = torch.nn.Parameter(bias, requires_grad=False)
+            return lin
+        qw = proj.qw
+        sub = QuantizedWeight(payload=qw.payload[r0:r1], scales=qw.scales[r0:r1], scheme=qw.scheme,
+                              original_shape=(r1 - r0, qw.original_shape[1]),
+                              group_size=qw.group_size, in_features_padded=qw.in_features_padded)
+        return QuantizedLinear.from_quantized(sub, bias)
+
+    def _load(self, sd: Dict[str, torch.Tensor]) -> None:
+        dev = self.device
+        g = lambda k: sd[k].detach().to(dev, torch.float32)
+        self.embed = g("model.embed_tokens.weight").contiguous()
+        self.lm_head = (self.embed if ("lm_head.weight" not in sd or self.cfg.tie_embeddings)
+                        else g("lm_head.weight").contiguous())
+        self.norm_w = g("model.norm.weight").contiguous()
+        qs, kvs = self.cfg.q_size, self.cfg.kv_size
+        self.layers: List[_Layer] = []
+        for i in range(self.n_layers):
+            p = f"model.layers.{i}."
+            L = _Layer()
+            L.ln1 = g(p + "input_layernorm.weight").contiguous()
+            L.ln2 = g(p + "post_attention_layernorm.weight").contiguous()
+            wq, wk, wv = g(p + "self_attn.q_proj.weight"), g(p + "self_attn.k_proj.weight"), g(
+                p + "self_attn.v_proj.weight")
+            L.qkv = self._pack(torch.cat([wq, wk, wv], dim=0))
+            bq = sd.get(p + "self_attn.q_proj.bias")
+            if bq is not None:
+                L.qkv.bias = torch.cat([g(p + "self_attn.q_proj.bias"), g(p + "self_attn.k_proj.bias"),
+                                        g(p + "self_attn.v_proj.bias")]).contiguous()
+            del wq, wk, wv
+            L.o = self._pack(g(p + "self_attn.o_proj.weight"))
+            L.gate_up = self._pack(torch.cat([g(p + "mlp.gate_proj.weight"),
+                                              g(p + "mlp.up_proj.weight")], dim=0))
+            L.down = self._pack(g(p + "mlp.down_proj.weight"))
+            b = L.qkv.bias
+            L.q_proj = self._view(L.qkv, 0, qs, None if b is None else b[:qs])
+            L.k_proj = self._view(L.qkv, qs, qs + kvs, None if b is None else b[qs:qs + kvs])
+            L.v_proj = self._view(L.qkv, qs + kvs, qs + 2 * kvs, None if b is None else b[qs + kvs:])
+            L.o_proj = self._view(L.o, 0, self.hidden)
+            L.gate_proj = self._view(L.gate_up, 0, self.inter)
+            L.up_proj = self._view(L.gate_up, self.inter, 2 * self.inter)
+            L.down_proj = self._view(L.down, 0, self.hidden)
+            self.layers.append(L)
+        torch.cuda.synchronize(dev)
+
+    def weight_bytes(self) -> Dict[str, int]:
+        """Bytes one decode step streams, by kind (algorithmic HBM traffic)."""
+        def pb(p: _Proj) -> int:
+            if p.qw is not None:
+                return p.qw.storage_bytes()
+            return p.w.numel() * 4
+        layers = sum(pb(L.qkv) + pb(L.o) + pb(L.gate_up) + pb(L.down) for L in self.layers)
+        return {"layers": layers, "lm_head": self.lm_head.numel() * 4}
+
+    # ------------------------------------------------------------------ #
+    # RoPE
+    # ------------------------------------------------------------------ #
+
+    @property
+    def rope_theta(self) -> float:
+        return self._rope_theta
+
+    @rope_theta.setter
+    def rope_theta(self, v: float) -> None:
+        self._rope_theta = float(v)
+        self._rope = None
+
+    def _rope_tables(self):
+        if self._rope is None:
+            c, s = rope_tables(self.head_dim, self._rope_theta, self.max_positions)
+            self._rope = (c.to(self.device), s.to(self.device))
+        return self._rope
+
+    # ------------------------------------------------------------------ #
+    # core: one pass over a varlen batch of token rows
+    # ------------------------------------------------------------------ #
+
+    def _alloc_acts(self, T: int) -> Dict[str, torch.Tensor]:
+        dev, f = self.device, torch.float32
+        return dict(
+            hidden=torch.empty((T, self.hidden), dtype=f, device=dev),
+            xn=torch.empty((T, self.hidden), dtype=f, device=dev),
+            qkv=torch.empty((T, self.cfg.q_size + 2 * self.cfg.kv_size), dtype=f, device=dev),
+            q=torch.empty((T, self.n_heads, self.head_dim), dtype=f, device=dev),
+            attn=torch.empty((T, self.n_heads, self.head_dim), dtype=f, device=dev),
+            h=torch.empty((T, self.inter), dtype=f, device=dev),
+        )
+
+    def _run_layers(self, acts, ids, positions, slots, block_tables, q_start, prefix_lens,
+                    num_seqs: int, max_q_len: int, max_total_len: int, pool: torch.Tensor,
+                    lin_ws: Workspace, attn_ws: AttentionWorkspace) -> torch.Tensor:
+        T = ids.shape[0]
+        s = stream_ptr()
+        hid, xn, qkv, q, attn, h = (acts[k] for k in ("hidden", "xn", "qkv", "q", "attn", "h"))
+        nb, L, _, hkv, bs, d = pool.shape
+        if pool.dtype != torch.float32 or not pool.is_contiguous():
+            raise ValueError("the pool must be a contiguous fp32 CUDA tensor")
+        rc, rs = self._rope_tables()
+        call("ksh_embedding", ptr(ids), T, ptr(self.embed), self.vocab_size, self.hidden, ptr(hid),
+             ptr(self.flags), s)
+        for i, Ly in enumerate(self.layers):
+            call("ksh_rmsnorm", ptr(hid), ptr(Ly.ln1), ptr(xn), T, self.hidden, self.eps, s)
+            linear_launch(xn, Ly.qkv.qw, Ly.qkv.w, Ly.qkv.bias, qkv, ws=lin_ws)
+            call("ksh_rope_kv_write", ptr(qkv), T, self.n_heads, self.n_kv_heads, self.head_dim,
+                 ptr(positions), ptr(slots), ptr(rc), ptr(rs), rc.shape[0], ptr(q), ptr(pool),
+                 nb, L, i, bs, ptr(self.flags), s)
+            paged_attention(q, pool, i, block_tables, q_start, prefix_lens, max_q_len,
+                            max_total_len, attn, self.flags, ws=attn_ws)
+            linear_launch(attn.view(T, -1), Ly.o.qw, Ly.o.w, None, hid, residual=hid, ws=lin_ws)
+            call("ksh_rmsnorm", ptr(hid), ptr(Ly.ln2), ptr(xn), T, self.hidden, self.eps, s)
+            swiglu_launch(xn, Ly.gate_up.qw, Ly.gate_up.w, self.inter, h, ws=lin_ws)
+            linear_launch(h, Ly.down.qw, Ly.down.w, None, hid, residual=hid, ws=lin_ws)
+        call("ksh_rmsnorm", ptr(hid), ptr(self.norm_w), ptr(xn), T, self.hidden, self.eps, s)
+        return xn
+
+    def _lm_workspace(self, m: int) -> torch.Tensor:
+        need = int(_lib.lib().ksh_lm_head_workspace_size(m, self.vocab_size))
+        if self._lm_ws is None or self._lm_ws.numel() < need:
+            self._lm_ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        return self._lm_ws
+
+    def _lm_head_argmax(self, x: torch.Tensor, tokens: torch.Tensor,
+                        ws: Optional[torch.Tensor] = None, logits: Optional[torch.Tensor] = None):
+        m = x.shape[0]
+        if ws is None:
+            ws = self._lm_workspace(m)
+        call("ksh_lm_head_argmax", ptr(x), m, self.hidden, ptr(self.lm_head), self.vocab_size,
+             ptr(logits), ptr(tokens), ptr(ws), ws.numel(), stream_ptr())
+
+    # ------------------------------------------------------------------ #
+    # reference API
+    # ------------------------------------------------------------------ #
+
+    @torch.inference_mode()
+    def forward(self, input_ids: torch.Tensor, position_ids: torch.Tensor, pool: torch.Tensor,
+                block_table: List[int], slot_mapping: List[int], prefix_len: int) -> torch.Tensor:
+        """Logits [1, L, vocab]; writes the chunk's K/V into ``pool``."""
+        assert input_ids.shape[0] == 1, "KshipraModel expects batch=1"
+        L = input_ids.shape[1]
+        dev = self.device
+        with torch.cuda.device(dev):
+            ids = input_ids.reshape(-1).to(dev, torch.int64)
+            pos = position_ids.reshape(-1).to(dev, torch.int64)
+            slots = torch.as_tensor(list(slot_mapping), dtype=torch.int64).to(dev)
+            bs = pool.shape[4]
+            nblk = (prefix_len + L + bs - 1) // bs
+            bt = torch.as_tensor([list(block_table)[:max(nblk, 1)]], dtype=torch.int32).to(dev)
+            q_start = torch.tensor([0, L], dtype=torch.int32, device=dev)
+            pl = torch.tensor([prefix_len], dtype=torch.int32, device=dev)
+            acts = self._alloc_acts(L)
+            xn = self._run_layers(acts, ids, pos, slots, bt, q_start, pl, 1, L, prefix_len + L,
+                                  pool, self._lin_ws, self._attn_ws)
+            logits = torch.empty((L, self.vocab_size), dtype=torch.float32, device=dev)
+            linear_launch(xn, None, self.lm_head, None, logits, ws=self._lin_ws)
+            _check_flags(self.flags)
+        return logits.view(1, L, self.vocab_size)
+
+    def new_pool(self, num_blocks: int, block_size: int) -> BlockAllocator:
+        return BlockAllocator(num_blocks=num_blocks, block_size=block_size, num_layers=self.n_layers,
+                              num_kv_heads=self.n_kv_heads, head_dim=self.head_dim,
+                              dtype=torch.float32, device=self.device)
+
+    @torch.inference_mode()
+    def prefill(self, prompt_ids: Sequence[int], pool: torch.Tensor, block_table: List[int],
+                prefill_chunk: Optional[int] = None, start: int = 0) -> torch.Tensor:
+        """Chunked prefill of ``prompt_ids[start:]``; returns the greedy next token [1] (device)."""
+        dev = self.device
+        bs = pool.shape[4]
+        lp = len(prompt_ids)
+        chunk = prefill_chunk or (lp - start)
+        bt = torch.as_tensor([list(block_table)], dtype=torch.int32).to(dev)
+        ids_all = torch.as_tensor(list(prompt_ids), dtype=torch.int64).to(dev)
+        pos_all = torch.arange(lp, dtype=torch.int64, device=dev)
+        bl = torch.as_tensor(list(block_table), dtype=torch.int64)
+        p = torch.arange(lp)
+        slots_all = (bl[p // bs] * bs + p % bs).to(dev)
+        tok = torch.empty(1, dtype=torch.int64, device=dev)
+        acts = self._alloc_acts(min(chunk, lp - start) if lp > start else 1)
+        pos = start
+        while pos < lp:
+            c = min(chunk, lp - pos)
+            a = acts if c == acts["hidden"].shape[0] else self._alloc_acts(c)
+            q_start = torch.tensor([0, c], dtype=torch.int32, device=dev)
+            pl = torch.tensor([pos], dtype=torch.int32, device=dev)
+            xn = self._run_layers(a, ids_all[pos:pos + c], pos_all[pos:pos + c],
+                                  slots_all[pos:pos + c], bt, q_start, pl, 1, c, pos + c, pool,
+                                  self._lin_ws, self._attn_ws)
+            pos += c
+        self._lm_head_argmax(xn[-1:], tok)
+        return tok
+
+    @torch.inference_mode()
+    def generate(self, prompt_ids: List[int], max_new_tokens: int = 20,
+                 eos_token_id: Optional[int] = None, block_size: int = 64,
+                 prefill_chunk: Optional[int] = None, use_graph: bool = True) -> List[int]:
+        """Greedy generation; returns the new token ids (model.py:154-205)."""
+        lp = len(prompt_ids)
+        nb = (lp + max_new_tokens + block_size - 1) // block_size
+        with torch.cuda.device(self.device):
+            alloc = self.new_pool(nb, block_size)
+            bt = list(range(nb))
+            first = self.prefill(prompt_ids, alloc.pool, bt, prefill_chunk)
+            hist = self.decode(first, lp, alloc.pool, bt, max_new_tokens, use_graph=use_graph)
+            _check_flags(self.flags)
+            toks = hist.tolist()
+        if eos_token_id is not None and eos_token_id in toks:
+            toks = toks[: toks.index(eos_token_id) + 1]
+        return toks
+
+    # ------------------------------------------------------------------ #
+    # decode loop (single sequence) with CUDA-graph replay
+    # ------------------------------------------------------------------ #
+
+    @torch.inference_mode()
+    def decode(self, first_tok: torch.Tensor, prompt_len: int, pool: torch.Tensor,
+               block_table: List[int], max_new_tokens: int, use_graph: bool = True) -> torch.Tensor:
+        """Greedy decode after a prefill: returns all ``max_new_tokens`` tokens
+        (the first one included) as a device tensor, host-synchronised."""
+        st = DecodeState(self, pool, [list(block_table)], max_new_tokens)
+        st.start(first_tok.view(1), [prompt_len])
+        steps = max_new_tokens - 1
+        if steps > 0:
+            st.step_eager()
+            if use_graph and steps > 1:
+                g = st.capture()
+                for _ in range(steps - 1):
+                    g.replay()
+            else:
+                for _ in range(steps - 1):
+                    st.step_eager()
+        torch.cuda.current_stream().synchronize()
+        return st.history[0, :max_new_tokens].cpu()
+
+
+class DecodeState:
+    """Static device buffers for batched greedy decode (graph-capturable).
+
+    Per sequence b: ids[b] (last token), positions[b] (its position),
+    prefix_lens[b] (= position: tokens already in the pool), slots[b], a row
+    of block_tables; ``history[b, step]`` collects generated tokens.
+    """
+
+    def __init__(self, model: KshipraModel, pool: torch.Tensor, block_tables: List[List[int]],
+                 max_new_tokens: int):
+        dev = model.device
+        self.m = model
+        self.pool = pool
+        B = len(block_tables)
+        maxb = max(len(r) for r in block_tables)
+        bt = torch.zeros((B, maxb), dtype=torch.int32)
+        for i, r in enumerate(block_tables):
+            bt[i, :len(r)] = torch.tensor(r, dtype=torch.int32)
+        self.B = B
+        self.block_tables = bt.to(dev)
+        self.capacity = maxb * pool.shape[4]
+        self.ids = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.positions = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.prefix_lens = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.slots = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.q_start = torch.arange(B + 1, dtype=torch.int32, device=dev)
+        self.next = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.history = torch.zeros((B, max(max_new_tokens, 1)), dtype=torch.int64, device=dev)
+        self.step_ctr = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.acts = model._alloc_acts(B)
+        self.lin_ws = Workspace()
+        self.attn_ws = AttentionWorkspace()
+        nbytes = int(_lib.lib().ksh_paged_attention_workspace_size(
+            B, model.n_heads, model.n_kv_heads, model.head_dim, 1, self.capacity))
+        self.attn_ws.get(nbytes, dev)
+        self.lm_ws = torch.zeros(int(_lib.lib().ksh_lm_head_workspace_size(B, model.vocab_size)),
+                                 dtype=torch.uint8, device=dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+
+    def start(self, first_tokens: torch.Tensor, prompt_lens: List[int]) -> None:
+        """Seed with each sequence's first generated token (from prefill)."""
+        self.next.copy_(first_tokens.view(-1))
+        self.positions.copy_(torch.tensor([p - 1 for p in prompt_lens], dtype=torch.int64))
+        self.step_ctr.zero_()
+        self._advance()
+
+    def _advance(self) -> None:
+        call("ksh_decode_advance", ptr(self.next), self.B, ptr(self.ids), ptr(self.positions),
+             ptr(self.prefix_lens), ptr(self.slots), ptr(self.block_tables),
+             self.block_tables.shape[1], self.pool.shape[4], ptr(self.history),
+             self.history.shape[1], ptr(self.step_ctr), ptr(self.m.flags), stream_ptr())
+
+    def _step(self) -> None:
+        m = self.m
+        xn = m._run_layers(self.acts, self.ids, self.positions, self.slots, self.block_tables,
+                           self.q_start, self.prefix_lens, self.B, 1, self.capacity, self.pool,
+                           self.lin_ws, self.attn_ws)
+        m._lm_head_argmax(xn, self.next, ws=self.lm_ws)
+        self._advance()
+
+    def step_eager(self) -> None:
+        self._step()
+
+    def capture(self) -> torch.cuda.CUDAGraph:
+        if self.graph is None:
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream(device=self.m.device)
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    self._step()
+            torch.cuda.current_stream().wait_stream(s)
+            self.graph = g
+        return self.graph

@@ -1,0 +1,137 @@
+"""End-to-end parity of the B200 forward with the reference (golden fixtures).
+
+* greedy token streams must match the reference bit-exactly;
+* logits must match within 1e-3 relative (max-abs error / max-abs logit),
+  the bound the path's specification states for fp32 accumulation.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from kshipra_b200.config import QWEN25_05B, TINY_LLAMA
+from kshipra_b200.model import KshipraModel
+from kshipra_b200.weights import build_hf_model, synthetic_state_dict
+from oracle.model import OracleModel
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_RTOL = 1e-3
+
+
+def logit_err(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / np.abs(b).max())
+
+
+@pytest.fixture(scope="module")
+def tiny_sd():
+    return synthetic_state_dict(TINY_LLAMA, seed=0)
+
+
+@pytest.mark.parametrize("scheme", ["int8", "int4", "none"])
+def test_tiny_generate_matches_reference(golden, tiny_sd, scheme):
+    g = golden("model_tiny.npz")
+    q = None if scheme == "none" else scheme
+    km = KshipraModel(config=TINY_LLAMA, state_dict=tiny_sd, quantize=q)
+    prompt = g["prompt"].tolist()
+    toks = km.generate(prompt, max_new_tokens=16, block_size=16, prefill_chunk=16)
+    assert toks == g[f"{scheme}/tokens"].tolist()
+    # eager decode (no graph) and one-shot prefill give the same stream
+    assert km.generate(prompt, 16, block_size=16, use_graph=False) == toks
+    assert g[f"{scheme}/tokens_oneshot"].tolist() == toks
+
+
+@pytest.mark.parametrize("scheme", ["int8", "int4"])
+def test_tiny_forward_logits_match_reference(golden, tiny_sd, scheme):
+    """The reference-facing forward(): chunked prefill then decode, logits per step."""
+    g = golden("model_tiny.npz")
+    km = KshipraModel(config=TINY_LLAMA, state_dict=tiny_sd, quantize=scheme)
+    prompt = g["prompt"].tolist()
+    ref_logits = g[f"{scheme}/logits"]
+    ref_toks = g[f"{scheme}/tokens"].tolist()
+    B = 16
+    alloc = km.new_pool((len(prompt) + 16 + B - 1) // B, B)
+    bt = list(range(alloc.pool.shape[0]))
+    pos = 0
+    while pos < len(prompt):
+        c = min(16, len(prompt) - pos)
+        ids = torch.tensor([prompt[pos:pos + c]])
+        positions = torch.arange(pos, pos + c).unsqueeze(0)
+        slots = [bt[p // B] * B + p % B for p in range(pos, pos + c)]
+        logits = km.forward(ids, positions, alloc.pool, bt, slots, prefix_len=pos)
+        pos += c
+    assert logit_err(logits[0, -1].cpu(), ref_logits[0]) < LOGIT_RTOL
+    toks = [int(logits[0, -1].argmax())]
+    for step in range(1, 16):
+        p = len(prompt) + step - 1
+        logits = km.forward(torch.tensor([[toks[-1]]]), torch.tensor([[p]]), alloc.pool, bt,
+                            [bt[p // B] * B + p % B], prefix_len=p)
+        assert logit_err(logits[0, -1].cpu(), ref_logits[step]) < LOGIT_RTOL
+        toks.append(int(logits[0, -1].argmax()))
+    assert toks == ref_toks
+
+
+def test_drop_in_from_hf_model(golden, tiny_sd):
+    """KshipraModel(hf_model, device, quantize) as the reference constructs it."""
+    g = golden("model_tiny.npz")
+    hf = build_hf_model(TINY_LLAMA, tiny_sd)
+    km = KshipraModel(hf, torch.device("cuda"), "int8")
+    km.rope_theta = TINY_LLAMA.rope_theta
+    toks = km.generate(g["prompt"].tolist(), max_new_tokens=16, block_size=16)
+    assert toks == g["int8/tokens"].tolist()
+    assert km.layers[0].q_proj.weight.payload.shape == (256, 256)
+    y = km.layers[0].k_proj(torch.randn(3, 256, device="cuda"))
+    assert tuple(y.shape) == (3, 128)
+
+
+def test_forward_matches_oracle_with_prefix(tiny_sd):
+    """forward() over a shuffled block table with a prefix, vs the oracle."""
+    gen = torch.Generator().manual_seed(0)
+    km = KshipraModel(config=TINY_LLAMA, state_dict=tiny_sd, quantize="int4")
+    orc = OracleModel(TINY_LLAMA, tiny_sd, "int4")
+    B = 8
+    nb = 12
+    bt = torch.randperm(nb, generator=gen).tolist()
+    ids = torch.randint(0, TINY_LLAMA.vocab, (1, 60), generator=gen)
+    alloc = km.new_pool(nb, B)
+    opool = orc.new_pool(nb, B)
+    for (a, b) in ((0, 23), (23, 41), (41, 42), (42, 60)):
+        positions = torch.arange(a, b).unsqueeze(0)
+        slots = [bt[p // B] * B + p % B for p in range(a, b)]
+        got = km.forward(ids[:, a:b], positions, alloc.pool, bt, slots, prefix_len=a).cpu()
+        ref = orc.forward(ids[:, a:b], positions, opool, bt, slots, prefix_len=a)
+        assert logit_err(got, ref) < LOGIT_RTOL
+        assert logit_err(got, ref) < 1e-5
+    np.testing.assert_allclose(alloc.pool.cpu().numpy(), opool.numpy(), rtol=1e-5, atol=1e-5)
+
+
+@pytest.fixture(scope="module")
+def qwen_sd():
+    return synthetic_state_dict(QWEN25_05B, seed=0)
+
+
+@pytest.mark.parametrize("scheme", ["int8", "int4"])
+def test_qwen05b_tokens_match_reference(golden, qwen_sd, scheme):
+    """Config: Qwen2.5-0.5B shape, 512-token prompt in 128-token chunks, 50 greedy tokens."""
+    g = golden("model_qwen05b.npz")
+    km = KshipraModel(config=QWEN25_05B, state_dict=qwen_sd, quantize=scheme)
+    prompt = g["prompt"].tolist()
+    toks = km.generate(prompt, max_new_tokens=50, block_size=16, prefill_chunk=128)
+    ref = g[f"{scheme}/tokens"].tolist()
+    if toks != ref:
+        i = next(i for i, (a, b) in enumerate(zip(toks, ref)) if a != b)
+        pytest.fail(f"first mismatch at {i}: margin there {g[f'{scheme}/margins'][i]}")
+    # logits after the prefill
+    B = 16
+    alloc = km.new_pool(33, B)
+    bt = list(range(33))
+    pos = 0
+    while pos < 512:
+        positions = torch.arange(pos, pos + 128).unsqueeze(0)
+        logits = km.forward(torch.tensor([prompt[pos:pos + 128]]), positions, alloc.pool, bt,
+                            list(range(pos, pos + 128)), prefix_len=pos)
+        pos += 128
+    err = logit_err(logits[0, -1].cpu(), g[f"{scheme}/logits0"])
+    assert err < LOGIT_RTOL, err
