@@ -333,6 +333,29 @@ def run_reference(args, wl):
     return res, rank
 
 
+def run_profile(args, wl):
+    """One request (chunked prefill + decode graph replays) between
+    cudaProfilerStart/Stop, after a warm-up, for ncu --profile-from-start off."""
+    from kshipra_b200.config import PRESETS
+    from kshipra_b200.model import KshipraModel
+    from kshipra_b200.weights import synthetic_state_dict
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = PRESETS[wl["preset"]]
+    km = KshipraModel(config=cfg, state_dict=synthetic_state_dict(cfg, 0, dev),
+                      quantize=wl["quantize"], device=dev)
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab, (wl["prompt"],), generator=g).tolist()
+    for _ in range(2):
+        km.generate(prompt, wl["new"], block_size=wl["block"], prefill_chunk=wl["chunk"])
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    toks = km.generate(prompt, wl["new"], block_size=wl["block"], prefill_chunk=wl["chunk"])
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"profile": args.workload, "tokens": len(toks)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -341,8 +364,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="qwen05b-int8", choices=sorted(WORKLOADS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="run one request inside cudaProfilerStart/Stop (for ncu)")
     args = ap.parse_args()
     wl = WORKLOADS[args.workload]
+    if args.profile:
+        run_profile(args, wl)
+        return
     if args.impl == "reference":
         res, rank = run_reference(args, wl)
     else:

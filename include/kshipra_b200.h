@@ -41,6 +41,7 @@ extern "C" {
 #define KSH_FLAG_BAD_POSITION  8   /* position outside the RoPE table */
 #define KSH_FLAG_BAD_TOKEN    16   /* token id outside [0, vocab) */
 #define KSH_FLAG_BAD_LENGTH   32   /* sequence longer than its block table */
+#define KSH_FLAG_TIMEOUT      64   /* a bounded device wait gave up */
 
 int ksh_abi_version(void);
 const char* ksh_status_string(int status);

@@ -1,28 +1,559 @@
 // K5: prefill / batched quantized GEMM on the tcgen05 tensor cores.
-// (Path selection lives in linear_api.cu; shapes this file does not take fall
-// back to the CUDA-core GEMM.)
+//
+// Replaces QuantizedLinear.forward (engine/quantization.py:394-396) for
+// M > 16 rows.  y[m, n] = sum_k x[m, k] * q[n, k] * s[n(, g)] (+ bias,
+// + residual, or SwiGLU over gate/up rows), x fp32.
+//
+// Precision scheme (the reference computes in fp32):
+//   * x is split per row into two fp16 terms after an exact power-of-two row
+//     scaling (x * 2^e = hi + lo, |x * 2^e| < 2^15), i.e. ~22 significant bits;
+//   * the quantized weights are small integers, exact in fp16;
+//   * D = hi * q^T + lo * q^T accumulates in fp32 in TMEM (two MMAs per K step);
+//   * scales are applied in fp32 outside the MMA: per output channel at the
+//     end (INT8), or per 128-wide K group by promoting each group's TMEM
+//     partial into register accumulators (INT4); the row factor 2^-e last.
+//
+// CTA = one 128 x 128 output tile (SwiGLU: 64 gate + 64 up rows of W), K
+// walked in 64-wide tiles through a 3-stage shared-memory ring:
+//   warp 0  : TMA producer (x hi / lo tiles with 128B swizzle, raw weight tile)
+//   warp 1  : TMEM allocation + single-thread tcgen05.mma issue
+//   warps 2-5: dequantize the raw weight tile to fp16 in the UMMA K-major
+//             128B-swizzled layout, then the epilogue (tcgen05.ld -> scales ->
+//             bias / residual / SwiGLU -> global)
+// Split-K over CTAs writes fp32 partial tiles to the workspace; the last CTA
+// of a tile sums them in split order (deterministic) and runs the epilogue.
+// Every mbarrier wait is bounded; a timeout raises KSH_FLAG_TIMEOUT in the
+// status word and the CTA unwinds (TMEM is always released).
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
 
 #include "linear.cuh"
+#include "tc_common.cuh"
 
 namespace ksh {
+namespace {
+
+using namespace tc;
+
+constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3;
+constexpr int kThreads = 192;
+constexpr int kMaxSplits = 8;
+constexpr uint32_t kTmemCols = 2 * BN;
+constexpr int A_BYTES = BM * BK * 2;      // one fp16 term
+constexpr int BH_BYTES = BN * BK * 2;     // dequantized fp16 B tile
+constexpr int BRAW_BYTES = BN * BK;       // int8 raw tile (int4 uses half)
+constexpr int STAGE_BYTES = 2 * A_BYTES + BH_BYTES + BRAW_BYTES;
+constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 256;
+
+struct TcArgs {
+  const __half* scales;
+  const float* bias;
+  const float* residual;
+  const float* inv_row;     // [M] 2^-e per x row
+  float* y;
+  float* part;              // split-K partial tiles
+  uint32_t* counters;       // per output tile, zero on entry
+  int32_t* flags;
+  int m, n, inter, kt_total, kt_per_split, kt_per_group, ngroups_row, g;
+};
+
+__device__ __forceinline__ float weight_scale(const TcArgs& a, int wk, int row, int kgroup) {
+  if (row < 0) return 0.0f;
+  if (wk == WK_I8) return __half2float(a.scales[row]);
+  return __half2float(a.scales[static_cast<int64_t>(row) * a.ngroups_row + kgroup]);
+}
+
+// int8 byte -> fp16 bits, exact: 0x6400 | (b ^ 0x80) = 1024 + b + 128.
+__device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t w, int byte0) {
+  const uint32_t x = w ^ 0x80808080u;
+  const uint32_t sel = static_cast<uint32_t>(byte0) | (4u << 4) | (static_cast<uint32_t>(byte0 + 1) << 8) |
+                       (5u << 12);
+  const uint32_t h = __byte_perm(x, 0x64646464u, sel);
+  __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __halves2half2(__ushort_as_half(0x6480),
+                                                                             __ushort_as_half(0x6480)));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+// two int4 nibbles (k, k+1) -> fp16 bits: 0x6400 | (u ^ 8) = 1024 + q + 8.
+__device__ __forceinline__ uint32_t i4x2_to_h2(uint32_t w, int nib0) {
+  const uint32_t lo = ((w >> (4 * nib0)) & 0xFu) ^ 0x8u;
+  const uint32_t hi = ((w >> (4 * nib0 + 4)) & 0xFu) ^ 0x8u;
+  const uint32_t h = (lo | 0x6400u) | ((hi | 0x6400u) << 16);
+  __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __halves2half2(__ushort_as_half(0x6408),
+                                                                             __ushort_as_half(0x6408)));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+template <int WK, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constant__ CUtensorMap map_xl,
+                const __grid_constant__ CUtensorMap map_w, TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* st_base = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;                 // [STAGES] TMA landed
+  uint64_t* bready = bars + STAGES;      // [STAGES] fp16 B tile written
+  uint64_t* empty = bars + 2 * STAGES;   // [STAGES] MMA done with the stage
+  uint64_t* acc_full = bars + 3 * STAGES;      // [2]
+  uint64_t* acc_empty = bars + 3 * STAGES + 2; // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y, split = blockIdx.z;
+  const int m0 = m_tile * BM;
+  const int kt_begin = split * a.kt_per_split;
+  const int kt_end = min(kt_begin + a.kt_per_split, a.kt_total);
+  const int ntl = max(kt_end - kt_begin, 0);
+  const int ktpg = WK == WK_I4 ? a.kt_per_group : max(ntl, 1);
+  const int ngl = (ntl + ktpg - 1) / ktpg;
+
+  auto stage_ah = [&](int s) { return st_base + s * STAGE_BYTES; };
+  auto stage_al = [&](int s) { return st_base + s * STAGE_BYTES + A_BYTES; };
+  auto stage_bh = [&](int s) { return st_base + s * STAGE_BYTES + 2 * A_BYTES; };
+  auto stage_br = [&](int s) { return st_base + s * STAGE_BYTES + 2 * A_BYTES + BH_BYTES; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&bready[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&map_xh);
+    prefetch_tmap(&map_xl);
+    prefetch_tmap(&map_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // Inputs (x split, weights) may be produced by the previous kernel.
+  grid_dep_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t bytes = 2 * A_BYTES + (WK == WK_I8 ? BN * BK : BN * BK / 2);
+      for (int i = 0; i < ntl && !*abort_flag; ++i) {
+        const int s = i % STAGES;
+        if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], bytes);
+        const int kg = (kt_begin + i) * BK;
+        tma_load_2d(stage_ah(s), &map_xh, &full[s], kg, m0);
+        tma_load_2d(stage_al(s), &map_xl, &full[s], kg, m0);
+        const int xw = WK == WK_I8 ? kg : kg / 2;
+        if (EPI == EPI_SWIGLU) {
+          const int half_bytes = (WK == WK_I8 ? BK : BK / 2) * (BN / 2);
+          tma_load_2d(stage_br(s), &map_w, &full[s], xw, n_tile * (BN / 2));
+          tma_load_2d(stage_br(s) + half_bytes, &map_w, &full[s], xw, a.inter + n_tile * (BN / 2));
+        } else {
+          tma_load_2d(stage_br(s), &map_w, &full[s], xw, n_tile * BN);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16_f32(BM, BN);
+      for (int i = 0; i < ntl && !*abort_flag; ++i) {
+        const int s = i % STAGES;
+        const int gl = i / ktpg, buf = gl & 1;
+        const bool first = (i % ktpg) == 0;
+        if (first && gl >= 2 && !mbar_wait(&acc_empty[buf], ((gl >> 1) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (!mbar_wait(&bready[s], (i / STAGES) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ah = smem_u32(stage_ah(s)), al = smem_u32(stage_al(s)),
+                       bh = smem_u32(stage_bh(s));
+        const uint32_t d = tmem + buf * BN;
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          const uint64_t bd = desc_k_sw128(bh + kk * 32);
+          mma_f16(d, desc_k_sw128(ah + kk * 32), bd, idesc, (first && kk == 0) ? 0u : 1u);
+          mma_f16(d, desc_k_sw128(al + kk * 32), bd, idesc, 1u);
+        }
+        mma_commit(&empty[s]);
+        if ((i % ktpg) == ktpg - 1 || i == ntl - 1) mma_commit(&acc_full[buf]);
+      }
+    }
+  } else {
+    // ---------------- converter + epilogue warps (128 threads) ----------------
+    const int t = threadIdx.x - 64;          // B tile row this thread converts
+    const int q = warp & 3;                  // TMEM lane quadrant of this warp
+    const int row_local = q * 32 + lane;     // accumulator row (TMEM lane)
+    float acc[BN];
+#pragma unroll
+    for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
+    // Weight row feeding accumulator column j (for scales); -1 if out of range.
+    auto wrow = [&](int j) -> int {
+      if (EPI == EPI_SWIGLU) {
+        const int c = n_tile * (BN / 2) + (j & (BN / 2 - 1));
+        if (c >= a.inter) return -1;
+        return j < BN / 2 ? c : a.inter + c;
+      }
+      const int r = n_tile * BN + j;
+      return r < a.n ? r : -1;
+    };
+    auto promote = [&](int gl) -> bool {
+      const int buf = gl & 1;
+      if (!mbar_wait(&acc_full[buf], (gl >> 1) & 1)) return false;
+      tc_fence_after();
+      const int kgroup = WK == WK_I4 ? (kt_begin + gl * ktpg) / ktpg : 0;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld_32x32b_x32(tmem + buf * BN + c * 32 + (static_cast<uint32_t>(q * 32) << 16), v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[c * 32 + j] = fmaf(v[j], weight_scale(a, WK, wrow(c * 32 + j), kgroup), acc[c * 32 + j]);
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+      return true;
+    };
+
+    bool ok = true;
+    for (int i = 0; i < ntl && ok; ++i) {
+      const int s = i % STAGES;
+      if (*abort_flag || !mbar_wait(&full[s], (i / STAGES) & 1)) {
+        ok = false;
+        break;
+      }
+      // dequantize row t of the raw tile into the 128B-swizzled fp16 tile
+      uint8_t* bh = stage_bh(s);
+      const uint32_t rsw = static_cast<uint32_t>(t & 7);
+      uint8_t* dst_row = bh + (t >> 3) * 1024 + (t & 7) * 128;
+      if (WK == WK_I8) {
+        const uint4* src = reinterpret_cast<const uint4*>(stage_br(s) + t * BK);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = (jj + (t >> 1)) & 3;           // rotate: conflict-free reads
+          const uint4 w = src[j];
+          uint4 o0, o1;
+          o0.x = i8x2_to_h2(w.x, 0); o0.y = i8x2_to_h2(w.x, 2);
+          o0.z = i8x2_to_h2(w.y, 0); o0.w = i8x2_to_h2(w.y, 2);
+          o1.x = i8x2_to_h2(w.z, 0); o1.y = i8x2_to_h2(w.z, 2);
+          o1.z = i8x2_to_h2(w.w, 0); o1.w = i8x2_to_h2(w.w, 2);
+          *reinterpret_cast<uint4*>(dst_row + (((2 * j) ^ rsw) << 4)) = o0;
+          *reinterpret_cast<uint4*>(dst_row + (((2 * j + 1) ^ rsw) << 4)) = o1;
+        }
+      } else {
+        const uint4* src = reinterpret_cast<const uint4*>(stage_br(s) + t * (BK / 2));
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j = (jj + (t >> 2)) & 1;
+          const uint4 w = src[j];
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {              // 8 nibbles -> one 16-byte chunk
+            uint4 o;
+            o.x = i4x2_to_h2(ws[e], 0);
+            o.y = i4x2_to_h2(ws[e], 2);
+            o.z = i4x2_to_h2(ws[e], 4);
+            o.w = i4x2_to_h2(ws[e], 6);
+            *reinterpret_cast<uint4*>(dst_row + ((static_cast<uint32_t>(4 * j + e) ^ rsw) << 4)) = o;
+          }
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bready[s]);
+      if (WK == WK_I4 && (i % ktpg) == ktpg - 1) {
+        const int gl = i / ktpg;
+        if (gl >= 1 && !promote(gl - 1)) ok = false;
+      }
+    }
+    if (ok && ntl > 0 && !*abort_flag) ok = promote(ngl - 1);
+    if (!ok) {
+      *abort_flag = 1;
+      raise_flag(a.flags, KSH_FLAG_TIMEOUT);
+    }
+
+    // ---------------- output ----------------
+    const int m = m0 + row_local;
+    const float inv = (m < a.m) ? a.inv_row[m] : 0.0f;
+    const int tiles = gridDim.x * gridDim.y;
+    const int tile = m_tile * gridDim.x + n_tile;
+    bool do_final = true;
+    if (gridDim.z > 1) {
+      float* mine = a.part + ((static_cast<int64_t>(split) * tiles + tile) * BM + row_local) * BN;
+#pragma unroll
+      for (int j = 0; j < BN; j += 4)
+        *reinterpret_cast<float4*>(mine + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (t == 0) *last_flag = (atomicAdd(a.counters + tile, 1u) == gridDim.z - 1) ? 1 : 0;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      do_final = *last_flag != 0;
+      if (do_final) {
+        __threadfence();
+#pragma unroll
+        for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
+        for (int sp = 0; sp < static_cast<int>(gridDim.z); ++sp) {
+          const float* p = a.part + ((static_cast<int64_t>(sp) * tiles + tile) * BM + row_local) * BN;
+#pragma unroll
+          for (int j = 0; j < BN; j += 4) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(p + j));
+            acc[j] += v.x; acc[j + 1] += v.y; acc[j + 2] += v.z; acc[j + 3] += v.w;
+          }
+        }
+        if (t == 0) a.counters[tile] = 0u;
+      }
+    }
+    if (do_final && m < a.m) {
+      if (EPI == EPI_SWIGLU) {
+        float* yr = a.y + static_cast<int64_t>(m) * a.inter;
+#pragma unroll
+        for (int j = 0; j < BN / 2; ++j) {
+          const int c = n_tile * (BN / 2) + j;
+          if (c < a.inter) {
+            const float gv = acc[j] * inv, uv = acc[BN / 2 + j] * inv;
+            yr[c] = silu_f(gv) * uv;
+          }
+        }
+      } else {
+        float* yr = a.y + static_cast<int64_t>(m) * a.n;
+        const float* rr = a.residual ? a.residual + static_cast<int64_t>(m) * a.n : nullptr;
+#pragma unroll
+        for (int j = 0; j < BN; ++j) {
+          const int c = n_tile * BN + j;
+          if (c < a.n) {
+            float v = acc[j] * inv;
+            if (a.bias) v += a.bias[c];
+            if (rr) v = rr[c] + v;
+            yr[c] = v;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+  grid_dep_launch();
+}
+
+// x fp32 [m, k] -> hi, lo fp16 [m, k] with a per-row power-of-two scale so
+// that max |x| * 2^e lies in [2^14, 2^15); inv_row[m] = 2^-e.
+__global__ void __launch_bounds__(256)
+split_x_kernel(const float* __restrict__ x, int64_t k, __half* __restrict__ xh,
+               __half* __restrict__ xl, float* __restrict__ inv_row) {
+  __shared__ float red[8];
+  grid_dep_wait();
+  grid_dep_launch();
+  const int64_t r = blockIdx.x;
+  const float* xr = x + r * k;
+  float mx = 0.0f;
+  for (int64_t j = threadIdx.x; j < k; j += blockDim.x) mx = fmaxf(mx, fabsf(xr[j]));
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  mx = red[0];
+  int e = 0;
+  if (mx > 0.0f && isfinite(mx)) {
+    int ex;
+    frexpf(mx, &ex);                 // mx = f * 2^ex, f in [0.5, 1)
+    e = 15 - ex;                     // mx * 2^e in [2^14, 2^15)
+    e = max(-100, min(e, 100));
+  }
+  const float sc = ldexpf(1.0f, e);
+  if (threadIdx.x == 0) inv_row[r] = ldexpf(1.0f, -e);
+  for (int64_t j = threadIdx.x; j < k; j += blockDim.x) {
+    const float v = xr[j] * sc;
+    const __half h = __float2half_rn(v);
+    xh[r * k + j] = h;
+    xl[r * k + j] = __float2half_rn(v - __half2float(h));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
+              uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+
+int max_splits(int64_t m, int64_t n) {
+  const int64_t tiles = ((n + BN - 1) / BN) * ((m + BM - 1) / BM);
+  const int64_t want = (num_sms() + tiles - 1) / tiles;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, kMaxSplits)));
+}
+
+// Split-K counters sit at a fixed offset (the first kCounterBytes, zeroed
+// once by the caller and left zero by every call) so that calls of different
+// shapes sharing one workspace never see each other's data there.
+constexpr int64_t kCounterBytes = 64 * 1024;
+
+struct WsLayout {
+  int64_t counters, xh, xl, inv, part, total;
+};
+
+WsLayout ws_layout(int64_t m, int64_t k, int64_t n_rows) {
+  WsLayout w = {};
+  const int64_t tiles = ((n_rows + BN - 1) / BN) * ((m + BM - 1) / BM);
+  w.counters = 0;
+  w.xh = kCounterBytes;
+  w.xl = w.xh + align256(m * k * 2);
+  w.inv = w.xl + align256(m * k * 2);
+  w.part = w.inv + align256(m * 4);
+  const int sp = tiles * 4 <= kCounterBytes ? max_splits(m, n_rows) : 1;
+  w.total = w.part + (sp > 1 ? static_cast<int64_t>(sp) * tiles * BM * BN * 4 : 0);
+  return w;
+}
+
+struct TcPlan {
+  int tiles_n, tiles_m, kt_total, kt_per_group, splits, kt_per_split;
+};
+
+TcPlan plan(int wk, int64_t m, int64_t keff, int64_t n_rows, int64_t g) {
+  TcPlan p = {};
+  p.tiles_n = static_cast<int>((n_rows + BN - 1) / BN);
+  p.tiles_m = static_cast<int>((m + BM - 1) / BM);
+  p.kt_total = static_cast<int>((keff + BK - 1) / BK);
+  p.kt_per_group = wk == WK_I4 ? static_cast<int>(g / BK) : 1;
+  const int64_t tiles = static_cast<int64_t>(p.tiles_n) * p.tiles_m;
+  int splits = tiles * 4 <= kCounterBytes ? max_splits(m, n_rows) : 1;
+  // at least 4 K tiles per split, split boundaries on group boundaries
+  splits = std::min(splits, std::max(1, p.kt_total / 4));
+  int kps = (p.kt_total + splits - 1) / splits;
+  kps = (kps + p.kt_per_group - 1) / p.kt_per_group * p.kt_per_group;
+  p.kt_per_split = kps;
+  p.splits = (p.kt_total + kps - 1) / kps;
+  return p;
+}
+
+template <int WK, int EPI>
+int launch_tc(const LinArgs& a, char* ws, cudaStream_t stream) {
+  const int64_t keff = WK == WK_I4 ? a.kp : a.k;
+  const int64_t n_rows = a.n;   // SwiGLU: 2 * inter rows
+  const TcPlan p = plan(WK, a.m, keff, n_rows, a.g);
+  const WsLayout L = ws_layout(a.m, a.k, n_rows);
+  __half* xh = reinterpret_cast<__half*>(ws + L.xh);
+  __half* xl = reinterpret_cast<__half*>(ws + L.xl);
+  float* inv = reinterpret_cast<float*>(ws + L.inv);
+  int st = launch(split_x_kernel, dim3(static_cast<unsigned>(a.m)), dim3(256), 0, stream, a.x, a.k,
+                  xh, xl, inv);
+  if (st != KSH_OK) return st;
+  CUtensorMap mxh, mxl, mw;
+  if (!make_map(&mxh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, a.k, a.m, a.k * 2, BK, BM,
+                CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mxl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xl, a.k, a.m, a.k * 2, BK, BM,
+                CU_TENSOR_MAP_SWIZZLE_128B))
+    return KSH_ERR_CUDA;
+  const uint32_t box_rows = EPI == EPI_SWIGLU ? BN / 2 : BN;
+  const bool ok = WK == WK_I8
+                      ? make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.k, n_rows, a.k, BK,
+                                 box_rows, CU_TENSOR_MAP_SWIZZLE_NONE)
+                      : make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.kp / 2, n_rows,
+                                 a.kp / 2, BK / 2, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!ok) return KSH_ERR_CUDA;
+  TcArgs t = {};
+  t.scales = a.scales;
+  t.bias = a.bias;
+  t.residual = a.residual;
+  t.inv_row = inv;
+  t.y = a.y;
+  t.part = reinterpret_cast<float*>(ws + L.part);
+  t.counters = reinterpret_cast<uint32_t*>(ws + L.counters);
+  t.flags = nullptr;
+  t.m = static_cast<int>(a.m);
+  t.n = static_cast<int>(a.n);
+  t.inter = static_cast<int>(a.inter);
+  t.kt_total = p.kt_total;
+  t.kt_per_split = p.kt_per_split;
+  t.kt_per_group = p.kt_per_group;
+  t.ngroups_row = WK == WK_I4 ? static_cast<int>(a.kp / a.g) : 1;
+  t.g = static_cast<int>(a.g);
+  auto kern = qgemm_tc_kernel<WK, EPI>;
+  if (set_smem_optin(reinterpret_cast<const void*>(kern), SMEM_BYTES) != KSH_OK) return KSH_ERR_CUDA;
+  const unsigned gx = EPI == EPI_SWIGLU ? static_cast<unsigned>((a.inter + BN / 2 - 1) / (BN / 2))
+                                        : static_cast<unsigned>(p.tiles_n);
+  return launch(kern, dim3(gx, static_cast<unsigned>(p.tiles_m), static_cast<unsigned>(p.splits)),
+                dim3(kThreads), SMEM_BYTES, stream, mxh, mxl, mw, t);
+}
+
+}  // namespace
 
 int64_t gemm_tc_workspace_size(int64_t m, int64_t k, int64_t n) {
-  (void)m;
-  (void)k;
-  (void)n;
-  return 0;
+  if (m <= 16) return 0;
+  return ws_layout(m, k, n).total;
 }
 
 int launch_gemm_tc(int wk, int epi, const LinArgs& a, void* ws, int64_t ws_bytes,
                    cudaStream_t stream, bool* taken) {
-  (void)wk;
-  (void)epi;
-  (void)a;
-  (void)ws;
-  (void)ws_bytes;
-  (void)stream;
   *taken = false;
-  return KSH_OK;
+  if (wk != WK_I8 && wk != WK_I4) return KSH_OK;
+  if (a.m > 65535 * BM || a.n > INT32_MAX) return KSH_OK;
+  if ((reinterpret_cast<uintptr_t>(a.w) & 15) != 0) return KSH_OK;
+  if (wk == WK_I8 && a.k % 16 != 0) return KSH_OK;
+  if (wk == WK_I4 && (a.g % BK != 0 || (a.kp / 2) % 16 != 0)) return KSH_OK;
+  if (a.k % 8 != 0) return KSH_OK;
+  if (!encode_fn()) return KSH_OK;
+  const WsLayout L = ws_layout(a.m, a.k, a.n);
+  if (!ws || ws_bytes < L.total || (reinterpret_cast<uintptr_t>(ws) & 255) != 0) return KSH_OK;
+  *taken = true;
+  char* w = static_cast<char*>(ws);
+  if (wk == WK_I8) return epi == EPI_SWIGLU ? launch_tc<WK_I8, EPI_SWIGLU>(a, w, stream)
+                                            : launch_tc<WK_I8, EPI_STORE>(a, w, stream);
+  return epi == EPI_SWIGLU ? launch_tc<WK_I4, EPI_SWIGLU>(a, w, stream)
+                           : launch_tc<WK_I4, EPI_STORE>(a, w, stream);
 }
 
 }  // namespace ksh

@@ -120,6 +120,7 @@ class KshipraModel:
         self._lin_ws = Workspace()
         self._attn_ws = AttentionWorkspace()
         self._lm_ws: Optional[torch.Tensor] = None
+        self._gen_cache: Dict[tuple, tuple] = {}
         with torch.cuda.device(self.device):
             self._load(state_dict)
 
@@ -207,6 +208,7 @@ class KshipraModel:
     def rope_theta(self, v: float) -> None:
         self._rope_theta = float(v)
         self._rope = None
+        self._gen_cache.clear()      # captured graphs point at the old tables
 
     def _rope_tables(self):
         if self._rope is None:
@@ -340,10 +342,22 @@ class KshipraModel:
         lp = len(prompt_ids)
         nb = (lp + max_new_tokens + block_size - 1) // block_size
         with torch.cuda.device(self.device):
-            alloc = self.new_pool(nb, block_size)
-            bt = list(range(nb))
+            # The reference allocates a fresh zeroed pool per call; every slot
+            # the forward reads was written earlier in the same call, so a
+            # cached pool of the same shape is equivalent and keeps the
+            # captured decode graph valid across calls.
+            key = (nb, block_size, max_new_tokens)
+            cached = self._gen_cache.get(key) if use_graph else None
+            if cached is None:
+                alloc = self.new_pool(nb, block_size)
+                bt = list(range(nb))
+                st = DecodeState(self, alloc.pool, [bt], max_new_tokens)
+                if use_graph:
+                    self._gen_cache[key] = (alloc, bt, st)
+            else:
+                alloc, bt, st = cached
             first = self.prefill(prompt_ids, alloc.pool, bt, prefill_chunk)
-            hist = self.decode(first, lp, alloc.pool, bt, max_new_tokens, use_graph=use_graph)
+            hist = self._decode_with(st, first, lp, max_new_tokens, use_graph)
             _check_flags(self.flags)
             toks = hist.tolist()
         if eos_token_id is not None and eos_token_id in toks:
@@ -360,16 +374,22 @@ class KshipraModel:
         """Greedy decode after a prefill: returns all ``max_new_tokens`` tokens
         (the first one included) as a device tensor, host-synchronised."""
         st = DecodeState(self, pool, [list(block_table)], max_new_tokens)
+        return self._decode_with(st, first_tok, prompt_len, max_new_tokens, use_graph)
+
+    def _decode_with(self, st: "DecodeState", first_tok: torch.Tensor, prompt_len: int,
+                     max_new_tokens: int, use_graph: bool) -> torch.Tensor:
         st.start(first_tok.view(1), [prompt_len])
         steps = max_new_tokens - 1
         if steps > 0:
-            st.step_eager()
             if use_graph and steps > 1:
+                if st.graph is None:
+                    st.step_eager()          # first call: eager step, then capture
+                    steps -= 1
                 g = st.capture()
-                for _ in range(steps - 1):
+                for _ in range(steps):
                     g.replay()
             else:
-                for _ in range(steps - 1):
+                for _ in range(steps):
                     st.step_eager()
         torch.cuda.current_stream().synchronize()
         return st.history[0, :max_new_tokens].cpu()

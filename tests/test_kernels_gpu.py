@@ -273,3 +273,36 @@ def test_lm_head_argmax_first_index():
             _lib.call("ksh_lm_head_argmax", xc.data_ptr(), m, H, wc.data_ptr(), V, None,
                       tok2.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_ptr())
             assert tok2.cpu().tolist() == tok.cpu().tolist()
+
+
+@pytest.mark.parametrize("scheme", ["int8", "int4"])
+@pytest.mark.parametrize("m,k,n", [(128, 896, 1152), (512, 4864, 896), (130, 896, 9728),
+                                   (2048, 4096, 512)])
+def test_tensor_core_gemm_prefill_shapes(scheme, m, k, n):
+    """tcgen05 path at the prefill shapes: fp64 reference with the dequantized weight."""
+    from kshipra_b200.quantization import (linear_launch, quantize_int4_per_group,
+                                           quantize_int8_per_channel, swiglu_launch)
+    gen = torch.Generator().manual_seed(m + k + n)
+    x = torch.randn((m, k), generator=gen)
+    x[3] *= 1e-3                        # rows with very different magnitudes
+    x[5] *= 300.0
+    w = torch.randn((n, k), generator=gen) * 0.02
+    if scheme == "int8":
+        qw = quantize_int8_per_channel(w.cuda())
+        wd = oq.dequantize_int8(qw.payload.cpu().numpy(), qw.scales.cpu().numpy())
+    else:
+        qw = quantize_int4_per_group(w.cuda(), 128)
+        wd = oq.dequantize_int4(qw.payload.cpu().numpy(), qw.scales.cpu().numpy(), k, 128)
+    y = torch.empty((m, n), device="cuda")
+    linear_launch(x.cuda(), qw, None, None, y)
+    y64 = x.double().numpy() @ wd.astype(np.float64).T
+    err = np.abs(y.cpu().numpy() - y64) / (np.abs(x.double().numpy()).max(axis=1, keepdims=True)
+                                           * np.abs(wd).max() * np.sqrt(k))
+    assert err.max() < 1e-6, err.max()
+    if n % 2 == 0:
+        inter = n // 2
+        h = torch.empty((m, inter), device="cuda")
+        swiglu_launch(x.cuda(), qw, None, inter, h)
+        g, u = y64[:, :inter], y64[:, inter:]
+        h64 = g / (1 + np.exp(-g)) * u
+        assert np.abs(h.cpu().numpy() - h64).max() <= 1e-5 * max(np.abs(h64).max(), 1.0)
