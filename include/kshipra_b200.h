@@ -69,24 +69,30 @@ int ksh_pack_int4(const float* w, int64_t n, int64_t k, int64_t group_size,
 /* ------------------------------------------------------------------------
  * Linear layers (replace QuantizedLinear.forward, engine/quantization.py:
  * 394-396, and nn.Linear for unquantized weights):
- *   y[m, j] = sum_k x[m, k] * W[j, k] + bias[j] + residual[m, j]
+ *   y[m, j] = sum_k x'[m, k] * W[j, k] + bias[j] + residual[m, j]
  * x fp32 [m, k]; bias [n] or NULL; residual [m, n] or NULL (may alias y).
+ * norm_w [k] or NULL: when set, x' = RMSNorm(x) with that weight and
+ * norm_eps (LlamaRMSNorm, engine/model.py:113,146), fused into the load of
+ * x; when NULL, x' = x.
  * M <= 16 runs the decode GEMV; larger M the tensor-core GEMM, which needs
  * the workspace reported by ksh_linear_workspace_size (else NULL/0).
  * ---------------------------------------------------------------------- */
 int64_t ksh_linear_workspace_size(int64_t m, int64_t k, int64_t n);
 
-int ksh_qlinear_w8(const float* x, int64_t m, int64_t k, const int8_t* payload,
+int ksh_qlinear_w8(const float* x, int64_t m, int64_t k,
+                   const float* norm_w, float norm_eps, const int8_t* payload,
                    const uint16_t* scales, const float* bias, const float* residual,
                    float* y, int64_t n, void* workspace, int64_t workspace_bytes,
                    void* stream);
 
-int ksh_qlinear_w4(const float* x, int64_t m, int64_t k, const uint8_t* payload,
+int ksh_qlinear_w4(const float* x, int64_t m, int64_t k,
+                   const float* norm_w, float norm_eps, const uint8_t* payload,
                    const uint16_t* scales, int64_t group_size, int64_t k_padded,
                    const float* bias, const float* residual, float* y, int64_t n,
                    void* workspace, int64_t workspace_bytes, void* stream);
 
-int ksh_linear_f32(const float* x, int64_t m, int64_t k, const float* w,
+int ksh_linear_f32(const float* x, int64_t m, int64_t k,
+                   const float* norm_w, float norm_eps, const float* w,
                    const float* bias, const float* residual, float* y, int64_t n,
                    void* workspace, int64_t workspace_bytes, void* stream);
 
@@ -94,14 +100,17 @@ int ksh_linear_f32(const float* x, int64_t m, int64_t k, const float* w,
  * act(gate_proj(x)) * up_proj(x), called at engine/model.py:147):
  * the weight holds 2*inter rows, gate rows [0, inter) then up rows
  * [inter, 2*inter); h[m, j] = silu(g[m, j]) * u[m, j]. */
-int ksh_qlinear_swiglu_w8(const float* x, int64_t m, int64_t k, const int8_t* payload,
+int ksh_qlinear_swiglu_w8(const float* x, int64_t m, int64_t k,
+                   const float* norm_w, float norm_eps, const int8_t* payload,
                           const uint16_t* scales, float* h, int64_t inter,
                           void* workspace, int64_t workspace_bytes, void* stream);
-int ksh_qlinear_swiglu_w4(const float* x, int64_t m, int64_t k, const uint8_t* payload,
+int ksh_qlinear_swiglu_w4(const float* x, int64_t m, int64_t k,
+                   const float* norm_w, float norm_eps, const uint8_t* payload,
                           const uint16_t* scales, int64_t group_size, int64_t k_padded,
                           float* h, int64_t inter, void* workspace,
                           int64_t workspace_bytes, void* stream);
-int ksh_linear_swiglu_f32(const float* x, int64_t m, int64_t k, const float* w,
+int ksh_linear_swiglu_f32(const float* x, int64_t m, int64_t k,
+                   const float* norm_w, float norm_eps, const float* w,
                           float* h, int64_t inter, void* workspace,
                           int64_t workspace_bytes, void* stream);
 
@@ -151,12 +160,30 @@ int ksh_paged_attention(const float* q, int64_t hq, int64_t d, const float* pool
                         int64_t workspace_bytes, int32_t* flags, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Decode step fused: RoPE of the new token's q / k at positions[b], the K/V
+ * write into the pool at slot_mapping[b], and paged attention of the token
+ * over keys 0 .. positions[b] (replaces _apply_rope + the pool write,
+ * engine/model.py:108,121-129, and chunked_attention with chunk_len = 1,
+ * engine/chunked_prefill.py:93-140).  qkv [batch, (hq + 2*hkv) * d] as for
+ * ksh_rope_kv_write; out [batch, hq, d].  Needs block_size % 16 == 0 and
+ * d in {64, 128}; max_total_len bounds positions[b] + 1 (grid sizing).
+ * ---------------------------------------------------------------------- */
+int ksh_decode_attention(const float* qkv, int64_t batch, int64_t hq, int64_t hkv, int64_t d,
+                         const int64_t* positions, const int64_t* slot_mapping,
+                         const float* rope_cos, const float* rope_sin, int64_t max_pos,
+                         float* pool, int64_t num_blocks, int64_t num_layers, int64_t layer,
+                         int64_t block_size, const int32_t* block_tables, int64_t max_blocks,
+                         int64_t max_total_len, float* out, int32_t* flags, void* stream);
+
+/* ------------------------------------------------------------------------
  * lm_head (fp32, never quantized; engine/model.py:151) fused with the greedy
  * argmax of generate (model.py:187, 200; first index of the maximum, as
- * torch.argmax).  logits [m, vocab] may be NULL (argmax only).
+ * torch.argmax).  logits [m, vocab] may be NULL (argmax only); norm_w as for
+ * the linear layers (the final model.norm, model.py:150).
  * ---------------------------------------------------------------------- */
 int64_t ksh_lm_head_workspace_size(int64_t m, int64_t vocab);
-int ksh_lm_head_argmax(const float* x, int64_t m, int64_t hidden, const float* w,
+int ksh_lm_head_argmax(const float* x, int64_t m, int64_t hidden, const float* norm_w,
+                       float norm_eps, const float* w,
                        int64_t vocab, float* logits, int64_t* tokens, void* workspace,
                        int64_t workspace_bytes, void* stream);
 /* Row-wise argmax of materialised logits [m, vocab]. */

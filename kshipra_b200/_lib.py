@@ -32,12 +32,12 @@ SIGNATURES = {
     "ksh_pack_int8": (I32, [P, I64, I64, P, P, P, P]),
     "ksh_pack_int4": (I32, [P, I64, I64, I64, P, P, P, P]),
     "ksh_linear_workspace_size": (I64, [I64, I64, I64]),
-    "ksh_qlinear_w8": (I32, [P, I64, I64, P, P, P, P, P, I64, P, I64, P]),
-    "ksh_qlinear_w4": (I32, [P, I64, I64, P, P, I64, I64, P, P, P, I64, P, I64, P]),
-    "ksh_linear_f32": (I32, [P, I64, I64, P, P, P, P, I64, P, I64, P]),
-    "ksh_qlinear_swiglu_w8": (I32, [P, I64, I64, P, P, P, I64, P, I64, P]),
-    "ksh_qlinear_swiglu_w4": (I32, [P, I64, I64, P, P, I64, I64, P, I64, P, I64, P]),
-    "ksh_linear_swiglu_f32": (I32, [P, I64, I64, P, P, I64, P, I64, P]),
+    "ksh_qlinear_w8": (I32, [P, I64, I64, P, F32, P, P, P, P, P, I64, P, I64, P]),
+    "ksh_qlinear_w4": (I32, [P, I64, I64, P, F32, P, P, I64, I64, P, P, P, I64, P, I64, P]),
+    "ksh_linear_f32": (I32, [P, I64, I64, P, F32, P, P, P, P, I64, P, I64, P]),
+    "ksh_qlinear_swiglu_w8": (I32, [P, I64, I64, P, F32, P, P, P, I64, P, I64, P]),
+    "ksh_qlinear_swiglu_w4": (I32, [P, I64, I64, P, F32, P, P, I64, I64, P, I64, P, I64, P]),
+    "ksh_linear_swiglu_f32": (I32, [P, I64, I64, P, F32, P, P, I64, P, I64, P]),
     "ksh_embedding": (I32, [P, I64, P, I64, I64, P, P, P]),
     "ksh_rmsnorm": (I32, [P, P, P, I64, I64, F32, P]),
     "ksh_rope_kv_write": (I32, [P, I64, I64, I64, I64, P, P, P, P, I64, P, P, I64, I64, I64,
@@ -45,8 +45,10 @@ SIGNATURES = {
     "ksh_paged_attention_workspace_size": (I64, [I64, I64, I64, I64, I64, I64]),
     "ksh_paged_attention": (I32, [P, I64, I64, P, I64, I64, I64, I64, I64, P, I64, P, P, I64,
                                   I64, I64, P, P, I64, P, P]),
+    "ksh_decode_attention": (I32, [P, I64, I64, I64, I64, P, P, P, P, I64, P, I64, I64, I64,
+                                   I64, P, I64, I64, P, P, P]),
     "ksh_lm_head_workspace_size": (I64, [I64, I64]),
-    "ksh_lm_head_argmax": (I32, [P, I64, I64, P, I64, P, P, P, I64, P]),
+    "ksh_lm_head_argmax": (I32, [P, I64, I64, P, F32, P, I64, P, P, P, I64, P]),
     "ksh_argmax_rows": (I32, [P, I64, I64, P, P]),
     "ksh_decode_advance": (I32, [P, I64, P, P, P, P, P, I64, I64, P, I64, P, P, P]),
 }

@@ -38,13 +38,34 @@ __global__ void __launch_bounds__(TH) gemm_simt_kernel(LinArgs a) {
   const int64_t m0 = static_cast<int64_t>(blockIdx.y) * BM;
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * BN;
   const int64_t ncols = EPI == EPI_SWIGLU ? a.inter : a.n;
+  // Optional RMSNorm of the x rows (LlamaRMSNorm), one warp per row, fixed order.
+  __shared__ float inv_rms[BM];
+  if (a.norm_w) {
+    const int lane = tid & 31, wid = tid >> 5;
+    for (int r = wid; r < BM; r += TH / 32) {
+      const int64_t mm = m0 + r;
+      float s = 0.0f;
+      if (mm < a.m)
+        for (int64_t e = lane; e < a.k; e += 32) {
+          const float v = a.x[mm * a.k + e];
+          s = fmaf(v, v, s);
+        }
+      s = warp_sum(s);
+      if (lane == 0)
+        inv_rms[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, static_cast<float>(a.k)),
+                                                          a.norm_eps)));
+    }
+    __syncthreads();
+  }
   float acc0[4][4] = {}, acc1[4][4] = {};
   for (int64_t k0 = 0; k0 < a.k; k0 += BK) {
 #pragma unroll
     for (int i = 0; i < (BM * BK) / TH; ++i) {
       const int e = tid + i * TH, r = e / BK, c = e % BK;
       const int64_t mm = m0 + r, kk = k0 + c;
-      xs[c][r] = (mm < a.m && kk < a.k) ? a.x[mm * a.k + kk] : 0.0f;
+      float xv = (mm < a.m && kk < a.k) ? a.x[mm * a.k + kk] : 0.0f;
+      if (a.norm_w && mm < a.m && kk < a.k) xv = __fmul_rn(a.norm_w[kk], __fmul_rn(xv, inv_rms[r]));
+      xs[c][r] = xv;
       const int64_t nn = n0 + r;
       ws0[c][r] = nn < ncols ? load_w<WK>(a, nn, kk) : 0.0f;
       if constexpr (EPI == EPI_SWIGLU) ws1[c][r] = nn < ncols ? load_w<WK>(a, nn + a.inter, kk) : 0.0f;

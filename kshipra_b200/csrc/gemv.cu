@@ -7,15 +7,20 @@
 // weight stream:
 //
 // * each warp owns one output row (two for the fused gate/up + SwiGLU);
-//   lanes read the row with 128-bit non-allocating loads, kUnroll vectors in
-//   flight per lane, and reduce with warp shuffles;
+//   lanes read the row with 128-bit non-allocating loads and reduce with
+//   warp shuffles;
+// * the first row's weight vectors (up to kHoist per lane) are loaded into
+//   registers BEFORE the programmatic-launch wait: weights never depend on
+//   the previous kernel, so their DRAM latency overlaps the tail of the
+//   previous kernel (or, without PDL, the activation staging);
 // * the activation rows (fp32) are staged once per CTA in shared memory with
 //   an XOR swizzle that makes the per-lane float4 reads bank-conflict free;
+//   an optional RMSNorm (LlamaRMSNorm arithmetic, deterministic per-row
+//   reduction) is applied while staging, which removes the separate norm
+//   kernel in front of q/k/v, gate/up and lm_head;
 // * dequantization happens in registers: INT8 sums x*q and applies the
 //   per-row fp16 scale once; INT4 sums x*q per 32-nibble vector (one group
 //   slice) and applies the group scale per vector;
-// * before the programmatic-launch wait the CTA prefetches its weight rows
-//   into L2, so the weight fetch of layer i+1 overlaps the tail of layer i;
 // * the lm_head variant fuses the greedy argmax (first index of the maximum)
 //   with a last-CTA reduction over per-CTA partials.
 
@@ -30,7 +35,17 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr int kUnroll = 4;
+// Weight vectors per lane held in registers: the register budget scales with
+// the number of staged-x values one vector consumes (4 fp32 / 16 int8 / 32
+// int4 elements), so the counts are sized by elements, about 64 per lane and
+// row.  Bandwidth for long rows comes from the bulk L2 prefetch of the CTA's
+// rows, not from deep register pipelining.
+template <int WK>
+constexpr int unroll_count() { return WK == WK_F32 ? 4 : 2; }
+template <int WK, int EPI, int MT>
+constexpr int hoist_count() {
+  return (WK == WK_F32 ? 8 : (WK == WK_I8 ? 4 : 2)) / (EPI == EPI_SWIGLU || MT > 4 ? 2 : 1);
+}
 
 template <int WK>
 struct Vec;
@@ -71,7 +86,7 @@ __device__ __forceinline__ float s4f(uint32_t w, int t) {
 }
 
 // Dot product of one 16-byte weight vector (local vector index v within the
-// staged tile) with staged x row mm.
+// staged tile) with one staged x row.
 template <int WK>
 __device__ __forceinline__ float vec_dot(const uint4& w, int v, const float4* xr) {
   float s = 0.0f;
@@ -117,35 +132,93 @@ __device__ __forceinline__ int64_t row_bytes(const LinArgs& a) {
   return a.kp / 2;
 }
 
-// Stage x[:, k0 : k0 + kl] (kl multiple of 4) into xs, zero-filled beyond
-// the logical k and beyond m.
+// Per-row 1/rms of x (LlamaRMSNorm: 1 / sqrt(mean(x^2) + eps)), reduced in a
+// fixed order (lanes, then warps) so results are run-to-run deterministic.
+template <int MT>
+__device__ __forceinline__ void row_inv_rms(const LinArgs& a, float (*red)[MT], float* inv) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int mm = 0; mm < MT; ++mm) {
+    float s = 0.0f;
+    if (mm < a.m)
+      for (int64_t e = threadIdx.x; e < a.k; e += kThreads) {
+        const float v = a.x[mm * a.k + e];
+        s = fmaf(v, v, s);
+      }
+    s = warp_sum(s);
+    if (lane == 0) red[warp][mm] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x < MT) {
+    float t = 0.0f;
+    for (int w = 0; w < kWarps; ++w) t += red[w][threadIdx.x];
+    const float var = __fdiv_rn(t, static_cast<float>(a.k));
+    inv[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, a.norm_eps)));
+  }
+  __syncthreads();
+}
+
+// Stage x[:, k0 : k0 + kl] (kl multiple of 4) into xs, zero-filled beyond the
+// logical k and beyond m; RMSNorm applied when a.norm_w is set.
 template <int WK, int MT>
 __device__ __forceinline__ void stage_x(const LinArgs& a, float4* xs, int ktv, int64_t k0,
-                                        int kl) {
+                                        int kl, const float* inv) {
   float* xf = reinterpret_cast<float*>(xs);
   const int nel = MT * kl;
   for (int i = threadIdx.x; i < nel; i += kThreads) {
     const int mm = i / kl, e = i - mm * kl;
     const int64_t kk = k0 + e;
     float v = 0.0f;
-    if (mm < a.m && kk < a.k) v = a.x[mm * a.k + kk];
+    if (mm < a.m && kk < a.k) {
+      v = a.x[mm * a.k + kk];
+      if (a.norm_w) v = __fmul_rn(a.norm_w[kk], __fmul_rn(v, inv[mm]));
+    }
     xf[(mm * ktv + swz<WK>(e >> 2)) * 4 + (e & 3)] = v;
   }
 }
 
-// Accumulate rows r0 (and r1 for SwiGLU) over the staged tile.
+// Fold one weight vector (local index v) of rows r0 / r1 into the accumulators.
+template <int WK, int EPI, int MT>
+__device__ __forceinline__ void fold_vec(const LinArgs& a, const float4* xs, int ktv,
+                                         int64_t r0, int64_t r1, int64_t k0, int v,
+                                         const uint4& w0, const uint4& w1, float (&acc0)[MT],
+                                         float (&acc1)[MT]) {
+  constexpr int E = Vec<WK>::E;
+  float s0 = 1.0f, s1 = 1.0f;
+  if constexpr (WK == WK_I4) {
+    const int64_t ng = a.kp / a.g;
+    const int64_t grp = (k0 + static_cast<int64_t>(v) * E) / a.g;
+    s0 = __half2float(a.scales[r0 * ng + grp]);
+    if constexpr (EPI == EPI_SWIGLU) s1 = __half2float(a.scales[r1 * ng + grp]);
+  }
+#pragma unroll
+  for (int mm = 0; mm < MT; ++mm) {
+    const float4* xr = xs + mm * ktv;
+    const float d0 = vec_dot<WK>(w0, v, xr);
+    if constexpr (WK == WK_I4) acc0[mm] = fmaf(d0, s0, acc0[mm]);
+    else acc0[mm] += d0;
+    if constexpr (EPI == EPI_SWIGLU) {
+      const float d1 = vec_dot<WK>(w1, v, xr);
+      if constexpr (WK == WK_I4) acc1[mm] = fmaf(d1, s1, acc1[mm]);
+      else acc1[mm] += d1;
+    }
+  }
+}
+
+// Accumulate rows r0 (and r1 for SwiGLU) over local vectors [v_begin, nv) of
+// the staged tile, kUnroll vectors in flight per lane.
 template <int WK, int EPI, int MT>
 __device__ __forceinline__ void accumulate(const LinArgs& a, const float4* xs, int ktv,
                                            int64_t r0, int64_t r1, int64_t k0, int kl,
-                                           float (&acc0)[MT], float (&acc1)[MT]) {
+                                           int v_begin, float (&acc0)[MT], float (&acc1)[MT]) {
   constexpr int E = Vec<WK>::E;
   const int lane = threadIdx.x & 31;
   const int64_t rb = row_bytes<WK>(a);
   const char* w0 = static_cast<const char*>(a.w) + r0 * rb + (k0 / E) * 16;
   const char* w1 = static_cast<const char*>(a.w) + r1 * rb + (k0 / E) * 16;
   const int nv = kl / E;
-  const int64_t ng = WK == WK_I4 ? a.kp / a.g : 0;
-  for (int v0 = lane; v0 < nv; v0 += 32 * kUnroll) {
+  constexpr int kUnroll = unroll_count<WK>();
+  for (int v0 = v_begin + lane; v0 < nv; v0 += 32 * kUnroll) {
     uint4 wv0[kUnroll], wv1[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
@@ -158,26 +231,7 @@ __device__ __forceinline__ void accumulate(const LinArgs& a, const float4* xs, i
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const int v = v0 + 32 * u;
-      if (v < nv) {
-        float s0 = 1.0f, s1 = 1.0f;
-        if constexpr (WK == WK_I4) {
-          const int64_t grp = (k0 + static_cast<int64_t>(v) * E) / a.g;
-          s0 = __half2float(a.scales[r0 * ng + grp]);
-          if constexpr (EPI == EPI_SWIGLU) s1 = __half2float(a.scales[r1 * ng + grp]);
-        }
-#pragma unroll
-        for (int mm = 0; mm < MT; ++mm) {
-          const float4* xr = xs + mm * ktv;
-          const float d0 = vec_dot<WK>(wv0[u], v, xr);
-          if constexpr (WK == WK_I4) acc0[mm] = fmaf(d0, s0, acc0[mm]);
-          else acc0[mm] += d0;
-          if constexpr (EPI == EPI_SWIGLU) {
-            const float d1 = vec_dot<WK>(wv1[u], v, xr);
-            if constexpr (WK == WK_I4) acc1[mm] = fmaf(d1, s1, acc1[mm]);
-            else acc1[mm] += d1;
-          }
-        }
-      }
+      if (v < nv) fold_vec<WK, EPI, MT>(a, xs, ktv, r0, r1, k0, v, wv0[u], wv1[u], acc0, acc1);
     }
   }
 }
@@ -239,18 +293,37 @@ __device__ __forceinline__ void finish_row(const LinArgs& a, int64_t rg, float (
 }
 
 template <int WK, int EPI, int MT, bool ARGMAX>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 2)
 gemv_kernel(LinArgs a, int kt, int prefetch) {
+  constexpr int E = Vec<WK>::E;
   extern __shared__ float4 xs[];
-  const int warp = threadIdx.x >> 5;
+  __shared__ float red[kWarps][MT];
+  __shared__ float inv_rms[MT];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t nrg = EPI == EPI_SWIGLU ? a.inter : a.n;
   const int64_t keff = WK == WK_I4 ? a.kp : a.k;
   const int ktv = kt / 4;
+  const bool single = keff <= kt;
+  const int64_t rb = row_bytes<WK>(a);
+  const int64_t rg0 = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  const int nv_row = static_cast<int>(keff / E);
 
-  if (prefetch) {
-    // Weight rows of this CTA's first row group: constant data, safe to
-    // touch before the dependency wait.
-    const int64_t rb = row_bytes<WK>(a);
+  // ---- constant data, safe before the dependency wait ----
+  constexpr int kHoist = hoist_count<WK, EPI, MT>();
+  uint4 h0[kHoist], h1[kHoist];
+  if (single && rg0 < nrg) {
+    const char* w0 = static_cast<const char*>(a.w) + rg0 * rb;
+    const char* w1 = static_cast<const char*>(a.w) + (rg0 + a.inter) * rb;
+#pragma unroll
+    for (int u = 0; u < kHoist; ++u) {
+      const int v = lane + 32 * u;
+      if (v < nv_row) {
+        h0[u] = ld_stream(w0 + static_cast<int64_t>(v) * 16);
+        if constexpr (EPI == EPI_SWIGLU) h1[u] = ld_stream(w1 + static_cast<int64_t>(v) * 16);
+      }
+    }
+  }
+  if (prefetch && (!single || nv_row > 32 * kHoist)) {
     const int64_t r_lo = static_cast<int64_t>(blockIdx.x) * kWarps;
     if (r_lo < nrg) {
       const int64_t nr = nrg - r_lo < kWarps ? nrg - r_lo : kWarps;
@@ -264,24 +337,34 @@ gemv_kernel(LinArgs a, int kt, int prefetch) {
   grid_dep_wait();
   grid_dep_launch();
 
+  if (a.norm_w) row_inv_rms<MT>(a, red, inv_rms);
+
   Best best[MT];
 #pragma unroll
   for (int mm = 0; mm < MT; ++mm) best[mm] = Best{-FLT_MAX, INT32_MAX};
 
-  if (keff <= kt) {
-    stage_x<WK, MT>(a, xs, ktv, 0, static_cast<int>(keff));
+  if (single) {
+    stage_x<WK, MT>(a, xs, ktv, 0, static_cast<int>(keff), inv_rms);
     __syncthreads();
-    for (int64_t rg = static_cast<int64_t>(blockIdx.x) * kWarps + warp; rg < nrg;
-         rg += static_cast<int64_t>(gridDim.x) * kWarps) {
+    for (int64_t rg = rg0; rg < nrg; rg += static_cast<int64_t>(gridDim.x) * kWarps) {
       float acc0[MT], acc1[MT];
 #pragma unroll
       for (int mm = 0; mm < MT; ++mm) acc0[mm] = acc1[mm] = 0.0f;
       const int64_t r1 = EPI == EPI_SWIGLU ? rg + a.inter : rg;
-      accumulate<WK, EPI, MT>(a, xs, ktv, rg, r1, 0, static_cast<int>(keff), acc0, acc1);
+      int v_begin = 0;
+      if (rg == rg0) {
+#pragma unroll
+        for (int u = 0; u < kHoist; ++u) {
+          const int v = lane + 32 * u;
+          if (v < nv_row) fold_vec<WK, EPI, MT>(a, xs, ktv, rg, r1, 0, v, h0[u], h1[u], acc0, acc1);
+        }
+        v_begin = 32 * kHoist;
+      }
+      accumulate<WK, EPI, MT>(a, xs, ktv, rg, r1, 0, static_cast<int>(keff), v_begin, acc0, acc1);
       finish_row<WK, EPI, MT, ARGMAX>(a, rg, acc0, acc1, best);
     }
   } else {
-    const int64_t rg = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+    const int64_t rg = rg0;
     const bool active = rg < nrg;
     const int64_t r1 = EPI == EPI_SWIGLU ? rg + a.inter : rg;
     float acc0[MT], acc1[MT];
@@ -290,9 +373,9 @@ gemv_kernel(LinArgs a, int kt, int prefetch) {
     for (int64_t k0 = 0; k0 < keff; k0 += kt) {
       const int kl = static_cast<int>(keff - k0 < kt ? keff - k0 : kt);
       __syncthreads();
-      stage_x<WK, MT>(a, xs, ktv, k0, kl);
+      stage_x<WK, MT>(a, xs, ktv, k0, kl, inv_rms);
       __syncthreads();
-      if (active) accumulate<WK, EPI, MT>(a, xs, ktv, rg, r1, k0, kl, acc0, acc1);
+      if (active) accumulate<WK, EPI, MT>(a, xs, ktv, rg, r1, k0, kl, 0, acc0, acc1);
     }
     if (active) finish_row<WK, EPI, MT, ARGMAX>(a, rg, acc0, acc1, best);
   }
@@ -301,7 +384,6 @@ gemv_kernel(LinArgs a, int kt, int prefetch) {
     // CTA reduce: lane mm of each warp holds the warp's best for row mm.
     __shared__ Best sb[kWarps][MT];
     __shared__ bool is_last;
-    const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int mm = 0; mm < MT; ++mm)
       if (lane == mm) sb[warp][mm] = best[mm];
@@ -365,11 +447,10 @@ int launch_t(const LinArgs& a, cudaStream_t stream) {
   }
   const int64_t nrg = EPI == EPI_SWIGLU ? a.inter : a.n;
   int64_t grid = (nrg + kWarps - 1) / kWarps;
-  if (keff <= kt) {
-    // single tile: persistent row loop, at most one resident wave
+  if (keff <= kt && ARGMAX) {
+    // persistent row loop, at most one resident wave
     const int per_sm = static_cast<int>(std::min<int64_t>(8, (200 * 1024) / std::max<size_t>(smem, 1)));
-    const int64_t cap = static_cast<int64_t>(num_sms()) * std::max(per_sm, 1);
-    if (ARGMAX) grid = std::min(grid, cap);
+    grid = std::min(grid, static_cast<int64_t>(num_sms()) * std::max(per_sm, 1));
   }
   if (grid > INT32_MAX) return KSH_ERR_UNSUPPORTED;
   return launch(kern, dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem, stream, a,

@@ -18,6 +18,8 @@ struct LinArgs {
   int64_t g;             // INT4 group size
   const float* bias;     // [n] or nullptr
   const float* residual; // [m, n] or nullptr (may alias y)
+  const float* norm_w;   // [k]: RMSNorm of x folded into the load, or nullptr
+  float norm_eps;
   float* y;              // STORE: [m, n]; SWIGLU: [m, inter]
   int64_t n;             // rows of W (SWIGLU: 2 * inter)
   int64_t inter;         // SWIGLU only

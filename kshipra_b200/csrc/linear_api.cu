@@ -59,6 +59,11 @@ LinArgs base(const float* x, int64_t m, int64_t k, int64_t kp, const void* w,
   return a;
 }
 
+void set_norm(LinArgs& a, const float* norm_w, float eps) {
+  a.norm_w = norm_w;
+  a.norm_eps = eps;
+}
+
 }  // namespace
 }  // namespace ksh
 
@@ -68,19 +73,20 @@ extern "C" int64_t ksh_linear_workspace_size(int64_t m, int64_t k, int64_t n) {
   return gemm_tc_workspace_size(m, k, n);
 }
 
-extern "C" int ksh_qlinear_w8(const float* x, int64_t m, int64_t k, const int8_t* payload,
+extern "C" int ksh_qlinear_w8(const float* x, int64_t m, int64_t k, const float* norm_w, float norm_eps, const int8_t* payload,
                               const uint16_t* scales, const float* bias,
                               const float* residual, float* y, int64_t n, void* workspace,
                               int64_t workspace_bytes, void* stream) {
   KSH_CHECK_ARG(m >= 0 && k > 0 && n > 0 && x && payload && scales && y);
   if (m == 0) return KSH_OK;
   LinArgs a = base(x, m, k, k, payload, scales, 0, y, n);
+  set_norm(a, norm_w, norm_eps);
   a.bias = bias;
   a.residual = residual;
   return run_linear(WK_I8, EPI_STORE, a, workspace, workspace_bytes, stream);
 }
 
-extern "C" int ksh_qlinear_w4(const float* x, int64_t m, int64_t k, const uint8_t* payload,
+extern "C" int ksh_qlinear_w4(const float* x, int64_t m, int64_t k, const float* norm_w, float norm_eps, const uint8_t* payload,
                               const uint16_t* scales, int64_t group_size, int64_t k_padded,
                               const float* bias, const float* residual, float* y, int64_t n,
                               void* workspace, int64_t workspace_bytes, void* stream) {
@@ -89,34 +95,37 @@ extern "C" int ksh_qlinear_w4(const float* x, int64_t m, int64_t k, const uint8_
                 k_padded >= k && k_padded - k < group_size);
   if (m == 0) return KSH_OK;
   LinArgs a = base(x, m, k, k_padded, payload, scales, group_size, y, n);
+  set_norm(a, norm_w, norm_eps);
   a.bias = bias;
   a.residual = residual;
   return run_linear(WK_I4, EPI_STORE, a, workspace, workspace_bytes, stream);
 }
 
-extern "C" int ksh_linear_f32(const float* x, int64_t m, int64_t k, const float* w,
+extern "C" int ksh_linear_f32(const float* x, int64_t m, int64_t k, const float* norm_w, float norm_eps, const float* w,
                               const float* bias, const float* residual, float* y, int64_t n,
                               void* workspace, int64_t workspace_bytes, void* stream) {
   KSH_CHECK_ARG(m >= 0 && k > 0 && n > 0 && x && w && y);
   if (m == 0) return KSH_OK;
   LinArgs a = base(x, m, k, k, w, nullptr, 0, y, n);
+  set_norm(a, norm_w, norm_eps);
   a.bias = bias;
   a.residual = residual;
   return run_linear(WK_F32, EPI_STORE, a, workspace, workspace_bytes, stream);
 }
 
-extern "C" int ksh_qlinear_swiglu_w8(const float* x, int64_t m, int64_t k,
+extern "C" int ksh_qlinear_swiglu_w8(const float* x, int64_t m, int64_t k, const float* norm_w, float norm_eps,
                                      const int8_t* payload, const uint16_t* scales, float* h,
                                      int64_t inter, void* workspace, int64_t workspace_bytes,
                                      void* stream) {
   KSH_CHECK_ARG(m >= 0 && k > 0 && inter > 0 && x && payload && scales && h);
   if (m == 0) return KSH_OK;
   LinArgs a = base(x, m, k, k, payload, scales, 0, h, 2 * inter);
+  set_norm(a, norm_w, norm_eps);
   a.inter = inter;
   return run_linear(WK_I8, EPI_SWIGLU, a, workspace, workspace_bytes, stream);
 }
 
-extern "C" int ksh_qlinear_swiglu_w4(const float* x, int64_t m, int64_t k,
+extern "C" int ksh_qlinear_swiglu_w4(const float* x, int64_t m, int64_t k, const float* norm_w, float norm_eps,
                                      const uint8_t* payload, const uint16_t* scales,
                                      int64_t group_size, int64_t k_padded, float* h,
                                      int64_t inter, void* workspace, int64_t workspace_bytes,
@@ -126,16 +135,18 @@ extern "C" int ksh_qlinear_swiglu_w4(const float* x, int64_t m, int64_t k,
                 k_padded >= k && k_padded - k < group_size);
   if (m == 0) return KSH_OK;
   LinArgs a = base(x, m, k, k_padded, payload, scales, group_size, h, 2 * inter);
+  set_norm(a, norm_w, norm_eps);
   a.inter = inter;
   return run_linear(WK_I4, EPI_SWIGLU, a, workspace, workspace_bytes, stream);
 }
 
-extern "C" int ksh_linear_swiglu_f32(const float* x, int64_t m, int64_t k, const float* w,
+extern "C" int ksh_linear_swiglu_f32(const float* x, int64_t m, int64_t k, const float* norm_w, float norm_eps, const float* w,
                                      float* h, int64_t inter, void* workspace,
                                      int64_t workspace_bytes, void* stream) {
   KSH_CHECK_ARG(m >= 0 && k > 0 && inter > 0 && x && w && h);
   if (m == 0) return KSH_OK;
   LinArgs a = base(x, m, k, k, w, nullptr, 0, h, 2 * inter);
+  set_norm(a, norm_w, norm_eps);
   a.inter = inter;
   return run_linear(WK_F32, EPI_SWIGLU, a, workspace, workspace_bytes, stream);
 }
@@ -196,13 +207,15 @@ extern "C" int ksh_argmax_rows(const float* logits, int64_t m, int64_t vocab, in
                 static_cast<cudaStream_t>(stream), logits, vocab, out);
 }
 
-extern "C" int ksh_lm_head_argmax(const float* x, int64_t m, int64_t hidden, const float* w,
+extern "C" int ksh_lm_head_argmax(const float* x, int64_t m, int64_t hidden,
+                                  const float* norm_w, float norm_eps, const float* w,
                                   int64_t vocab, float* logits, int64_t* tokens,
                                   void* workspace, int64_t workspace_bytes, void* stream) {
   KSH_CHECK_ARG(m >= 0 && hidden > 0 && vocab > 0 && vocab <= INT32_MAX && x && w);
   KSH_CHECK_ARG(logits || tokens);
   if (m == 0) return KSH_OK;
   LinArgs a = base(x, m, hidden, hidden, w, nullptr, 0, logits, vocab);
+  set_norm(a, norm_w, norm_eps);
   if (tokens && gemv_ok(WK_F32, a)) {
     const int64_t need = ksh_lm_head_workspace_size(m, vocab);
     if (!workspace || workspace_bytes < need) return KSH_ERR_WORKSPACE;

@@ -358,17 +358,41 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
 }
 
 // x fp32 [m, k] -> hi, lo fp16 [m, k] with a per-row power-of-two scale so
-// that max |x| * 2^e lies in [2^14, 2^15); inv_row[m] = 2^-e.
+// that max |x| * 2^e lies in [2^14, 2^15); inv_row[m] = 2^-e.  With norm_w
+// set, x is first RMSNorm-ed (LlamaRMSNorm arithmetic, fixed-order reduction).
+__device__ __forceinline__ float norm_val(const float* xr, const float* norm_w, float inv,
+                                          int64_t j) {
+  const float v = xr[j];
+  return norm_w ? __fmul_rn(norm_w[j], __fmul_rn(v, inv)) : v;
+}
+
 __global__ void __launch_bounds__(256)
 split_x_kernel(const float* __restrict__ x, int64_t k, __half* __restrict__ xh,
-               __half* __restrict__ xl, float* __restrict__ inv_row) {
+               __half* __restrict__ xl, float* __restrict__ inv_row,
+               const float* __restrict__ norm_w, float eps) {
   __shared__ float red[8];
   grid_dep_wait();
   grid_dep_launch();
   const int64_t r = blockIdx.x;
   const float* xr = x + r * k;
+  float inv = 1.0f;
+  if (norm_w) {
+    float ss = 0.0f;
+    for (int64_t j = threadIdx.x; j < k; j += blockDim.x) ss = fmaf(xr[j], xr[j], ss);
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+      v = warp_sum(v);
+      if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], static_cast<float>(k)), eps)));
+    __syncthreads();
+  }
   float mx = 0.0f;
-  for (int64_t j = threadIdx.x; j < k; j += blockDim.x) mx = fmaxf(mx, fabsf(xr[j]));
+  for (int64_t j = threadIdx.x; j < k; j += blockDim.x) mx = fmaxf(mx, fabsf(norm_val(xr, norm_w, inv, j)));
   mx = warp_max(mx);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
   __syncthreads();
@@ -389,7 +413,7 @@ split_x_kernel(const float* __restrict__ x, int64_t k, __half* __restrict__ xh,
   const float sc = ldexpf(1.0f, e);
   if (threadIdx.x == 0) inv_row[r] = ldexpf(1.0f, -e);
   for (int64_t j = threadIdx.x; j < k; j += blockDim.x) {
-    const float v = xr[j] * sc;
+    const float v = norm_val(xr, norm_w, inv, j) * sc;
     const __half h = __float2half_rn(v);
     xh[r * k + j] = h;
     xl[r * k + j] = __float2half_rn(v - __half2float(h));
@@ -489,7 +513,7 @@ int launch_tc(const LinArgs& a, char* ws, cudaStream_t stream) {
   __half* xl = reinterpret_cast<__half*>(ws + L.xl);
   float* inv = reinterpret_cast<float*>(ws + L.inv);
   int st = launch(split_x_kernel, dim3(static_cast<unsigned>(a.m)), dim3(256), 0, stream, a.x, a.k,
-                  xh, xl, inv);
+                  xh, xl, inv, a.norm_w, a.norm_eps);
   if (st != KSH_OK) return st;
   CUtensorMap mxh, mxl, mw;
   if (!make_map(&mxh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, a.k, a.m, a.k * 2, BK, BM,

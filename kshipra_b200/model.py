@@ -46,6 +46,10 @@ FLAG_NAMES = {1: "non-finite weight", 2: "block id out of range", 4: "slot out o
               32: "sequence longer than its block table"}
 
 
+# GQA group sizes the fused decode-attention kernel is instantiated for, per head dim.
+_DECODE_GROUPS = {64: (1, 2, 4, 7, 8), 128: (1, 2, 4, 8)}
+
+
 class KshipraDeviceError(IndexError):
     """A kernel reported a data-dependent error through the device status word."""
 
@@ -121,6 +125,7 @@ class KshipraModel:
         self._attn_ws = AttentionWorkspace()
         self._lm_ws: Optional[torch.Tensor] = None
         self._gen_cache: Dict[tuple, tuple] = {}
+        self.fused_decode = True
         with torch.cuda.device(self.device):
             self._load(state_dict)
 
@@ -243,20 +248,30 @@ class KshipraModel:
         rc, rs = self._rope_tables()
         call("ksh_embedding", ptr(ids), T, ptr(self.embed), self.vocab_size, self.hidden, ptr(hid),
              ptr(self.flags), s)
+        eps = self.eps
+        # decode step (one token per sequence, position == prefix length): the
+        # fused RoPE + K/V write + attention kernel
+        fused = (max_q_len == 1 and T == num_seqs and self.fused_decode and bs % 16 == 0
+                 and d in (64, 128) and self.n_heads // self.n_kv_heads in _DECODE_GROUPS[d])
         for i, Ly in enumerate(self.layers):
-            call("ksh_rmsnorm", ptr(hid), ptr(Ly.ln1), ptr(xn), T, self.hidden, self.eps, s)
-            linear_launch(xn, Ly.qkv.qw, Ly.qkv.w, Ly.qkv.bias, qkv, ws=lin_ws)
-            call("ksh_rope_kv_write", ptr(qkv), T, self.n_heads, self.n_kv_heads, self.head_dim,
-                 ptr(positions), ptr(slots), ptr(rc), ptr(rs), rc.shape[0], ptr(q), ptr(pool),
-                 nb, L, i, bs, ptr(self.flags), s)
-            paged_attention(q, pool, i, block_tables, q_start, prefix_lens, max_q_len,
-                            max_total_len, attn, self.flags, ws=attn_ws)
+            linear_launch(hid, Ly.qkv.qw, Ly.qkv.w, Ly.qkv.bias, qkv, ws=lin_ws, norm_w=Ly.ln1,
+                          eps=eps)
+            if fused:
+                call("ksh_decode_attention", ptr(qkv), T, self.n_heads, self.n_kv_heads, d,
+                     ptr(positions), ptr(slots), ptr(rc), ptr(rs), rc.shape[0], ptr(pool), nb, L,
+                     i, bs, ptr(block_tables), block_tables.shape[1], max_total_len, ptr(attn),
+                     ptr(self.flags), s)
+            else:
+                call("ksh_rope_kv_write", ptr(qkv), T, self.n_heads, self.n_kv_heads,
+                     self.head_dim, ptr(positions), ptr(slots), ptr(rc), ptr(rs), rc.shape[0],
+                     ptr(q), ptr(pool), nb, L, i, bs, ptr(self.flags), s)
+                paged_attention(q, pool, i, block_tables, q_start, prefix_lens, max_q_len,
+                                max_total_len, attn, self.flags, ws=attn_ws)
             linear_launch(attn.view(T, -1), Ly.o.qw, Ly.o.w, None, hid, residual=hid, ws=lin_ws)
-            call("ksh_rmsnorm", ptr(hid), ptr(Ly.ln2), ptr(xn), T, self.hidden, self.eps, s)
-            swiglu_launch(xn, Ly.gate_up.qw, Ly.gate_up.w, self.inter, h, ws=lin_ws)
+            swiglu_launch(hid, Ly.gate_up.qw, Ly.gate_up.w, self.inter, h, ws=lin_ws,
+                          norm_w=Ly.ln2, eps=eps)
             linear_launch(h, Ly.down.qw, Ly.down.w, None, hid, residual=hid, ws=lin_ws)
-        call("ksh_rmsnorm", ptr(hid), ptr(self.norm_w), ptr(xn), T, self.hidden, self.eps, s)
-        return xn
+        return hid
 
     def _lm_workspace(self, m: int) -> torch.Tensor:
         need = int(_lib.lib().ksh_lm_head_workspace_size(m, self.vocab_size))
@@ -269,8 +284,9 @@ class KshipraModel:
         m = x.shape[0]
         if ws is None:
             ws = self._lm_workspace(m)
-        call("ksh_lm_head_argmax", ptr(x), m, self.hidden, ptr(self.lm_head), self.vocab_size,
-             ptr(logits), ptr(tokens), ptr(ws), ws.numel(), stream_ptr())
+        call("ksh_lm_head_argmax", ptr(x), m, self.hidden, ptr(self.norm_w), self.eps,
+             ptr(self.lm_head), self.vocab_size, ptr(logits), ptr(tokens), ptr(ws), ws.numel(),
+             stream_ptr())
 
     # ------------------------------------------------------------------ #
     # reference API
@@ -296,7 +312,8 @@ class KshipraModel:
             xn = self._run_layers(acts, ids, pos, slots, bt, q_start, pl, 1, L, prefix_len + L,
                                   pool, self._lin_ws, self._attn_ws)
             logits = torch.empty((L, self.vocab_size), dtype=torch.float32, device=dev)
-            linear_launch(xn, None, self.lm_head, None, logits, ws=self._lin_ws)
+            linear_launch(xn, None, self.lm_head, None, logits, ws=self._lin_ws,
+                          norm_w=self.norm_w, eps=self.eps)
             _check_flags(self.flags)
         return logits.view(1, L, self.vocab_size)
 

@@ -174,39 +174,47 @@ _WS = Workspace()
 
 def linear_launch(x2d: torch.Tensor, qw: Optional[QuantizedWeight], w_f32: Optional[torch.Tensor],
                   bias: Optional[torch.Tensor], out: torch.Tensor,
-                  residual: Optional[torch.Tensor] = None, ws: Workspace = _WS) -> torch.Tensor:
-    """out[m, n] = x2d @ W^T (+ bias) (+ residual), W quantized or fp32."""
+                  residual: Optional[torch.Tensor] = None, ws: Workspace = _WS,
+                  norm_w: Optional[torch.Tensor] = None, eps: float = 1e-6) -> torch.Tensor:
+    """out[m, n] = x' @ W^T (+ bias) (+ residual), W quantized or fp32;
+    x' = RMSNorm(x2d; norm_w, eps) when norm_w is given, else x2d."""
     m, k = x2d.shape
     n = out.shape[1]
     wsz = int(_lib.lib().ksh_linear_workspace_size(m, k, n))
     wp, wb = ws.get(wsz, x2d.device)
     s = stream_ptr()
+    nw = ptr(norm_w)
     if qw is None:
-        call("ksh_linear_f32", ptr(x2d), m, k, ptr(w_f32), ptr(bias), ptr(residual), ptr(out), n,
-             wp, wb, s)
+        call("ksh_linear_f32", ptr(x2d), m, k, nw, eps, ptr(w_f32), ptr(bias), ptr(residual),
+             ptr(out), n, wp, wb, s)
     elif qw.scheme == "int8_per_channel":
-        call("ksh_qlinear_w8", ptr(x2d), m, k, ptr(qw.payload), ptr(qw.scales), ptr(bias),
-             ptr(residual), ptr(out), n, wp, wb, s)
+        call("ksh_qlinear_w8", ptr(x2d), m, k, nw, eps, ptr(qw.payload), ptr(qw.scales),
+             ptr(bias), ptr(residual), ptr(out), n, wp, wb, s)
     else:
-        call("ksh_qlinear_w4", ptr(x2d), m, k, ptr(qw.payload), ptr(qw.scales), qw.group_size,
-             qw.in_features_padded, ptr(bias), ptr(residual), ptr(out), n, wp, wb, s)
+        call("ksh_qlinear_w4", ptr(x2d), m, k, nw, eps, ptr(qw.payload), ptr(qw.scales),
+             qw.group_size, qw.in_features_padded, ptr(bias), ptr(residual), ptr(out), n, wp,
+             wb, s)
     return out
 
 
 def swiglu_launch(x2d: torch.Tensor, qw: Optional[QuantizedWeight], w_f32: Optional[torch.Tensor],
-                  inter: int, out: torch.Tensor, ws: Workspace = _WS) -> torch.Tensor:
-    """out[m, j] = silu(x W_gate^T)[m, j] * (x W_up^T)[m, j]; W holds gate rows then up rows."""
+                  inter: int, out: torch.Tensor, ws: Workspace = _WS,
+                  norm_w: Optional[torch.Tensor] = None, eps: float = 1e-6) -> torch.Tensor:
+    """out[m, j] = silu(x' W_gate^T)[m, j] * (x' W_up^T)[m, j]; W holds gate rows then
+    up rows; x' = RMSNorm(x2d) when norm_w is given."""
     m, k = x2d.shape
     wsz = int(_lib.lib().ksh_linear_workspace_size(m, k, 2 * inter))
     wp, wb = ws.get(wsz, x2d.device)
     s = stream_ptr()
+    nw = ptr(norm_w)
     if qw is None:
-        call("ksh_linear_swiglu_f32", ptr(x2d), m, k, ptr(w_f32), ptr(out), inter, wp, wb, s)
+        call("ksh_linear_swiglu_f32", ptr(x2d), m, k, nw, eps, ptr(w_f32), ptr(out), inter, wp,
+             wb, s)
     elif qw.scheme == "int8_per_channel":
-        call("ksh_qlinear_swiglu_w8", ptr(x2d), m, k, ptr(qw.payload), ptr(qw.scales), ptr(out),
-             inter, wp, wb, s)
+        call("ksh_qlinear_swiglu_w8", ptr(x2d), m, k, nw, eps, ptr(qw.payload), ptr(qw.scales),
+             ptr(out), inter, wp, wb, s)
     else:
-        call("ksh_qlinear_swiglu_w4", ptr(x2d), m, k, ptr(qw.payload), ptr(qw.scales),
+        call("ksh_qlinear_swiglu_w4", ptr(x2d), m, k, nw, eps, ptr(qw.payload), ptr(qw.scales),
              qw.group_size, qw.in_features_padded, ptr(out), inter, wp, wb, s)
     return out
 

@@ -260,7 +260,7 @@ def test_lm_head_argmax_first_index():
         ws = torch.zeros(int(_lib.lib().ksh_lm_head_workspace_size(m, V)), dtype=torch.uint8,
                          device="cuda")
         wc, xc = w.cuda(), x.cuda()
-        _lib.call("ksh_lm_head_argmax", xc.data_ptr(), m, H, wc.data_ptr(), V,
+        _lib.call("ksh_lm_head_argmax", xc.data_ptr(), m, H, None, 0.0, wc.data_ptr(), V,
                   logits.data_ptr(), tok.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_ptr())
         ref = x.double() @ w.double().T
         lg = logits.cpu()
@@ -270,7 +270,7 @@ def test_lm_head_argmax_first_index():
         # argmax-only call (no logits) agrees
         tok2 = torch.empty(m, dtype=torch.int64, device="cuda")
         if m <= 16:
-            _lib.call("ksh_lm_head_argmax", xc.data_ptr(), m, H, wc.data_ptr(), V, None,
+            _lib.call("ksh_lm_head_argmax", xc.data_ptr(), m, H, None, 0.0, wc.data_ptr(), V, None,
                       tok2.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_ptr())
             assert tok2.cpu().tolist() == tok.cpu().tolist()
 
@@ -306,3 +306,55 @@ def test_tensor_core_gemm_prefill_shapes(scheme, m, k, n):
         g, u = y64[:, :inter], y64[:, inter:]
         h64 = g / (1 + np.exp(-g)) * u
         assert np.abs(h.cpu().numpy() - h64).max() <= 1e-5 * max(np.abs(h64).max(), 1.0)
+
+
+@pytest.mark.parametrize("D,hq,hkv,bs", [(64, 14, 2, 16), (64, 4, 2, 32), (128, 32, 8, 16),
+                                         (128, 8, 8, 64), (64, 8, 1, 16)])
+def test_fused_decode_attention_vs_oracle(D, hq, hkv, bs):
+    """RoPE + K/V write + attention of one new token per sequence, batched."""
+    from kshipra_b200 import _lib
+    from kshipra_b200.model import rope_tables
+    gen = torch.Generator().manual_seed(D + hq + bs)
+    positions = [0, 5, 15, 16, 100, 561, 1023]
+    B = len(positions)
+    L, layer = 2, 1
+    maxb = (max(positions) + 1 + bs - 1) // bs + 1
+    nb = B * maxb + 3
+    perm = torch.randperm(nb, generator=gen)
+    bt = perm[:B * maxb].view(B, maxb).to(torch.int32)
+    pool = torch.randn((nb, L, 2, hkv, bs, D), generator=gen)
+    qkv = torch.randn((B, (hq + 2 * hkv) * D), generator=gen)
+    rc, rs = rope_tables(D, 10000.0, 2048)
+    pos = torch.tensor(positions, dtype=torch.int64)
+    slots = torch.tensor([int(bt[b, p // bs]) * bs + p % bs for b, p in enumerate(positions)])
+    dev = [t.cuda() for t in (qkv, pos, slots, rc, rs, bt)]
+    poolc = pool.cuda()
+    out = torch.empty((B, hq, D), device="cuda")
+    flags = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.call("ksh_decode_attention", dev[0].data_ptr(), B, hq, hkv, D, dev[1].data_ptr(),
+              dev[2].data_ptr(), dev[3].data_ptr(), dev[4].data_ptr(), 2048, poolc.data_ptr(),
+              nb, L, layer, bs, dev[5].data_ptr(), maxb, max(positions) + 1, out.data_ptr(),
+              flags.data_ptr(), _lib.stream_ptr())
+    assert int(flags.item()) == 0
+    out = out.cpu()
+    pool_after = poolc.cpu()
+    ref_pool = pool          # block tables are disjoint: one reference pool serves all
+    qrs = []
+    for b, p in enumerate(positions):
+        cos, sin = om.compute_rope(D, torch.tensor([[p]]), 10000.0)
+        q = qkv[b, :hq * D].view(1, 1, hq, D).transpose(1, 2)
+        k = qkv[b, hq * D:(hq + hkv) * D].view(1, 1, hkv, D).transpose(1, 2)
+        v = qkv[b, (hq + hkv) * D:].view(hkv, D)
+        qr, kr = om.apply_rope(q, k, cos, sin)
+        qrs.append(qr)
+        s = int(slots[b])
+        ref_pool[s // bs, layer, 0, :, s % bs] = kr[0, :, 0]
+        ref_pool[s // bs, layer, 1, :, s % bs] = v
+        np.testing.assert_array_equal(pool_after[s // bs, layer, :, :, s % bs].numpy(),
+                                      ref_pool[s // bs, layer, :, :, s % bs].numpy())
+    for b, p in enumerate(positions):
+        qr = qrs[b]
+        ref = oa.chunked_attention(qr[0], ref_pool[:, layer, 0], ref_pool[:, layer, 1],
+                                   bt[b].tolist(), p, 1, bs)
+        got = out[b].unsqueeze(1)
+        assert rel_l2(got.numpy(), ref.numpy()) < 1e-5, (b, p, rel_l2(got.numpy(), ref.numpy()))
