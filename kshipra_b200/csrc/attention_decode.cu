@@ -103,20 +103,25 @@ __global__ void __launch_bounds__(kThreads)
 decode_attn_kernel(DecArgs a) {
   constexpr int D4 = D / 4;
   constexpr int TILE_F = kTK * D;               // floats per K (or V) tile
-  constexpr int GP = G < 8 ? 8 : G;             // padded head rows for the score layout
+  constexpr int CH = NST / 2;                   // tiles per chunk (ring = 2 chunks)
+  constexpr int CK = CH * kTK;                  // keys per chunk
+  constexpr int NPV = (G * D4 + kThreads - 1) / kThreads;   // (head, float4 col) pairs per thread
   extern __shared__ __align__(128) float4 sm4[];
   float* sm = reinterpret_cast<float*>(sm4);
   float* Kt = sm;                               // [NST][kTK][D]
   float* Vt = Kt + NST * TILE_F;                // [NST][kTK][D]
   float* Qs = Vt + NST * TILE_F;                // [G][D]
-  float* Ss = Qs + G * D;                       // [GP][kTK + 1]
-  float* corr_s = Ss + GP * (kTK + 1);          // [GP]
-  float* part = corr_s + GP;                    // [G][D + 4]: m, l, pad, pad, acc
+  float* Ss = Qs + G * D;                       // [G][CK + 1]
+  float* corr_s = Ss + G * (CK + 1);            // [G]
+  float* ms = corr_s + G;                       // [G] running max
+  float* ls = ms + G;                           // [G] running sum
+  // offsets so far: 2*NST*TILE_F + G*D + G*CK + 4G floats, a multiple of 4
+  float* part = ls + G;                         // [G][D + 4]: m, l, pad, pad, acc (16B aligned)
   uint64_t* full = reinterpret_cast<uint64_t*>(part + G * (D + 4));   // [NST]
   __shared__ int tile_ok[NST];
   __shared__ float newk[D], newv[D];
 
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t rank = cluster_rank(), csize = cluster_size();
   const int item = blockIdx.y;                  // (b, hk)
   const int b = item / static_cast<int>(a.hkv);
@@ -135,7 +140,7 @@ decode_attn_kernel(DecArgs a) {
   const int64_t head_rows = a.hkv * a.bs;                         // rows between K and V
   const int32_t* bt = a.block_tables + static_cast<int64_t>(b) * a.max_blocks;
 
-  auto issue = [&](int i) {          // tile t_begin + i into stage i % NST (thread 0)
+  auto issue = [&](int i) {          // local tile i into stage i % NST (thread 0)
     const int s = i % NST;
     const int t = t_begin + i;
     const int64_t j = (static_cast<int64_t>(t) * kTK) / a.bs;
@@ -158,6 +163,10 @@ decode_attn_kernel(DecArgs a) {
     for (int s = 0; s < NST; ++s) mbar_init(&full[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     for (int i = 0; i < ntl && i < NST; ++i) issue(i);
+  }
+  if (tid < G) {
+    ms[tid] = -INFINITY;
+    ls[tid] = 0.0f;
   }
 
   grid_dep_wait();
@@ -211,141 +220,163 @@ decode_attn_kernel(DecArgs a) {
     }
   }
 
-  // ---- tiles ----
-  float m_r = -INFINITY, l_r = 0.0f;             // softmax state of head tid (< G)
-  constexpr int RSTEP = kThreads / D4;           // heads per PV pass
-  constexpr int NRPV = (G + RSTEP - 1) / RSTEP;
-  const int c4 = tid % D4, h0 = tid / D4;
-  float4 acc[NRPV];
+  // ---- chunks of CH tiles ----
+  float4 acc[NPV];
 #pragma unroll
-  for (int i = 0; i < NRPV; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int u = 0; u < NPV; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
   bool timed_out = false, bad_block = false;
 
-  for (int i = 0; i < ntl; ++i) {
-    const int s = i % NST;
-    const int t = t_begin + i;
-    if (!mbar_wait(&full[s], (i / NST) & 1)) {
-      timed_out = true;
-      break;
+  for (int c0 = 0; c0 < ntl && !timed_out; c0 += CH) {
+    const int nt = min(CH, ntl - c0);
+    for (int i = c0; i < c0 + nt; ++i) {
+      if (!mbar_wait(&full[i % NST], (i / NST) & 1)) timed_out = true;
+      if (!tile_ok[i % NST]) bad_block = true;
     }
-    const float* Kc = Kt + s * TILE_F;
-    const float* Vc = Vt + s * TILE_F;
-    const bool ok = tile_ok[s] != 0;
-    if (!ok) bad_block = true;
-    if (owner && i == ntl - 1) {               // patch the new token's row
-      const int rr = static_cast<int>(p) - t * kTK;
+    if (timed_out) break;
+    if (owner && c0 + nt == ntl) {             // patch the new token's row
+      const int i = ntl - 1, s = i % NST;
+      const int rr = static_cast<int>(p) - (t_begin + i) * kTK;
       for (int j = tid; j < D; j += kThreads) {
         Kt[s * TILE_F + rr * D + j] = newk[j];
         Vt[s * TILE_F + rr * D + j] = newv[j];
       }
       __syncthreads();
     }
-    // scores: thread -> key j = tid & 15, heads tid >> 4, +8, ...
-    {
-      const int j = tid & (kTK - 1);
-      const int kpos = t * kTK + j;
+    const int kbase = (t_begin + c0) * kTK;    // absolute position of chunk key 0
+    const int nk = nt * kTK;
+    // scores S[h][j] = (q_h . k_j) * scale, -inf beyond the causal bound
+    for (int idx = tid; idx < G * CK; idx += kThreads) {
+      const int h = idx / CK, j = idx - h * CK;
+      float sc = -INFINITY;
+      const int s = (c0 + j / kTK) % NST;
+      if (j < nk && kbase + j < total_c && tile_ok[s]) {
+        const float* kr = Kt + s * TILE_F + (j % kTK) * D;
+        float dot = 0.0f;
 #pragma unroll
-      for (int hh = tid >> 4; hh < GP; hh += kThreads / kTK) {
-        float sc = -INFINITY;
-        if (hh < G && ok && kpos < total_c) {
-          float dot = 0.0f;
-#pragma unroll
-          for (int cc = 0; cc < D4; ++cc) {
-            const int c = (cc + j) & (D4 - 1);
-            const float4 qv = reinterpret_cast<const float4*>(Qs + hh * D)[c];
-            const float4 kv = reinterpret_cast<const float4*>(Kc + j * D)[c];
-            dot = fmaf(qv.x, kv.x, dot);
-            dot = fmaf(qv.y, kv.y, dot);
-            dot = fmaf(qv.z, kv.z, dot);
-            dot = fmaf(qv.w, kv.w, dot);
-          }
-          sc = dot * a.scale;
+        for (int cc = 0; cc < D4; ++cc) {
+          const int c = (cc + j) & (D4 - 1);
+          const float4 qv = reinterpret_cast<const float4*>(Qs + h * D)[c];
+          const float4 kv = reinterpret_cast<const float4*>(kr)[c];
+          dot = fmaf(qv.x, kv.x, dot);
+          dot = fmaf(qv.y, kv.y, dot);
+          dot = fmaf(qv.z, kv.z, dot);
+          dot = fmaf(qv.w, kv.w, dot);
         }
-        Ss[hh * (kTK + 1) + j] = sc;
+        sc = dot * a.scale;
       }
+      Ss[h * (CK + 1) + j] = sc;
     }
     __syncthreads();
-    if (tid < G) {
-      float* srow = Ss + tid * (kTK + 1);
+    // online softmax merge, one warp per head
+    for (int h = warp; h < G; h += kThreads / 32) {
+      float* srow = Ss + h * (CK + 1);
       float mx = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < kTK; ++j) mx = fmaxf(mx, srow[j]);
-      const float m_new = fmaxf(m_r, mx);
+      for (int j = lane; j < CK; j += 32) mx = fmaxf(mx, srow[j]);
+      mx = warp_max(mx);
+      const float m_old = ms[h];
+      const float m_new = fmaxf(m_old, mx);
       const float m_safe = isinf(m_new) ? 0.0f : m_new;
       float psum = 0.0f;
-#pragma unroll
-      for (int j = 0; j < kTK; ++j) {
+      for (int j = lane; j < CK; j += 32) {
         const float pj = expf(srow[j] - m_safe);
         srow[j] = pj;
         psum += pj;
       }
-      const float corr = expf(m_r - m_safe);
-      l_r = __fadd_rn(__fmul_rn(l_r, corr), psum);
-      m_r = m_new;
-      corr_s[tid] = corr;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int ii = 0; ii < NRPV; ++ii) {
-      const int h = h0 + RSTEP * ii;
-      if (h < G) {
-        const float* pr_ = Ss + h * (kTK + 1);
-        float4 pv = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int j = 0; j < kTK; ++j) {
-          const float pj = pr_[j];
-          const float4 v = reinterpret_cast<const float4*>(Vc + j * D)[c4];
-          pv.x = fmaf(pj, v.x, pv.x);
-          pv.y = fmaf(pj, v.y, pv.y);
-          pv.z = fmaf(pj, v.z, pv.z);
-          pv.w = fmaf(pj, v.w, pv.w);
-        }
-        const float crr = corr_s[h];
-        acc[ii].x = __fadd_rn(__fmul_rn(acc[ii].x, crr), pv.x);
-        acc[ii].y = __fadd_rn(__fmul_rn(acc[ii].y, crr), pv.y);
-        acc[ii].z = __fadd_rn(__fmul_rn(acc[ii].z, crr), pv.z);
-        acc[ii].w = __fadd_rn(__fmul_rn(acc[ii].w, crr), pv.w);
+      psum = warp_sum(psum);
+      if (lane == 0) {
+        const float corr = expf(m_old - m_safe);
+        ls[h] = __fadd_rn(__fmul_rn(ls[h], corr), psum);
+        ms[h] = m_new;
+        corr_s[h] = corr;
       }
     }
-    __syncthreads();                           // stage s fully consumed
-    if (tid == 0 && i + NST < ntl) issue(i + NST);
+    __syncthreads();
+    // acc[h][c4] = acc * corr[h] + sum_j p[h][j] V[j][c4]
+#pragma unroll
+    for (int u = 0; u < NPV; ++u) {
+      const int idx = tid + u * kThreads;
+      if (idx < G * D4) {
+        const int h = idx / D4, c4 = idx - h * D4;
+        const float* prow = Ss + h * (CK + 1);
+        float4 pv = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int t = 0; t < nt; ++t) {
+          const float* vt = Vt + ((c0 + t) % NST) * TILE_F;
+#pragma unroll
+          for (int jj = 0; jj < kTK; ++jj) {
+            const float pj = prow[t * kTK + jj];
+            const float4 v = reinterpret_cast<const float4*>(vt + jj * D)[c4];
+            pv.x = fmaf(pj, v.x, pv.x);
+            pv.y = fmaf(pj, v.y, pv.y);
+            pv.z = fmaf(pj, v.z, pv.z);
+            pv.w = fmaf(pj, v.w, pv.w);
+          }
+        }
+        const float crr = corr_s[h];
+        acc[u].x = __fadd_rn(__fmul_rn(acc[u].x, crr), pv.x);
+        acc[u].y = __fadd_rn(__fmul_rn(acc[u].y, crr), pv.y);
+        acc[u].z = __fadd_rn(__fmul_rn(acc[u].z, crr), pv.z);
+        acc[u].w = __fadd_rn(__fmul_rn(acc[u].w, crr), pv.w);
+      }
+    }
+    __syncthreads();                           // this chunk's stages are free
+    if (tid == 0)
+      for (int i = c0 + NST; i < min(c0 + NST + CH, ntl); ++i) issue(i);
   }
   if (tid == 0) {
     if (timed_out) raise_flag(a.flags, KSH_FLAG_TIMEOUT);
     if (bad_block) raise_flag(a.flags, KSH_FLAG_BAD_BLOCK);
   }
 
-  // ---- publish this CTA's state, merge across the cluster in rank order ----
+  // ---- publish this CTA's state; every rank merges a slice of the outputs ----
   if (tid < G) {
-    part[tid * (D + 4)] = m_r;
-    part[tid * (D + 4) + 1] = l_r;
+    part[tid * (D + 4)] = ms[tid];
+    part[tid * (D + 4) + 1] = ls[tid];
   }
 #pragma unroll
-  for (int ii = 0; ii < NRPV; ++ii) {
-    const int h = h0 + RSTEP * ii;
-    if (h < G) reinterpret_cast<float4*>(part + h * (D + 4) + 4)[c4] = acc[ii];
+  for (int u = 0; u < NPV; ++u) {
+    const int idx = tid + u * kThreads;
+    if (idx < G * D4) {
+      const int h = idx / D4, c4 = idx - h * D4;
+      reinterpret_cast<float4*>(part + h * (D + 4) + 4)[c4] = acc[u];
+    }
   }
   __syncthreads();
   cluster_sync();
-  if (rank == 0) {
+  {
     const uint32_t base = smem_u32(part);
-    for (int w = tid; w < G * D4; w += kThreads) {
+    const int per_rank = (G * D4 + static_cast<int>(csize) - 1) / static_cast<int>(csize);
+    for (int w = static_cast<int>(rank) * per_rank + tid;
+         w < min((static_cast<int>(rank) + 1) * per_rank, G * D4); w += kThreads) {
       const int h = w / D4, c = w - h * D4;
       const uint32_t off = static_cast<uint32_t>(h * (D + 4)) * 4u;
+      float mr[kMaxCluster], lr[kMaxCluster];
+      float4 ar[kMaxCluster];
+#pragma unroll
+      for (int r = 0; r < kMaxCluster; ++r) {
+        if (r < static_cast<int>(csize)) {
+          const uint32_t pb = map_rank(base + off, static_cast<uint32_t>(r));
+          mr[r] = ld_cluster_f32(pb);
+          lr[r] = ld_cluster_f32(pb + 4);
+          ar[r] = ld_cluster_f32x4(pb + 16u + static_cast<uint32_t>(c) * 16u);
+        }
+      }
       float M = -INFINITY;
-      for (uint32_t r = 0; r < csize; ++r) M = fmaxf(M, ld_cluster_f32(map_rank(base + off, r)));
+#pragma unroll
+      for (int r = 0; r < kMaxCluster; ++r)
+        if (r < static_cast<int>(csize)) M = fmaxf(M, mr[r]);
       const float Ms = isinf(M) ? 0.0f : M;
       float L = 0.0f;
       float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (uint32_t r = 0; r < csize; ++r) {
-        const uint32_t pb = map_rank(base + off, r);
-        const float wgt = expf(ld_cluster_f32(pb) - Ms);
-        L = fmaf(ld_cluster_f32(pb + 4), wgt, L);
-        const float4 ar = ld_cluster_f32x4(pb + 16u + static_cast<uint32_t>(c) * 16u);
-        A.x = fmaf(ar.x, wgt, A.x);
-        A.y = fmaf(ar.y, wgt, A.y);
-        A.z = fmaf(ar.z, wgt, A.z);
-        A.w = fmaf(ar.w, wgt, A.w);
+#pragma unroll
+      for (int r = 0; r < kMaxCluster; ++r) {
+        if (r < static_cast<int>(csize)) {
+          const float wgt = expf(mr[r] - Ms);
+          L = fmaf(lr[r], wgt, L);
+          A.x = fmaf(ar[r].x, wgt, A.x);
+          A.y = fmaf(ar[r].y, wgt, A.y);
+          A.z = fmaf(ar[r].z, wgt, A.z);
+          A.w = fmaf(ar[r].w, wgt, A.w);
+        }
       }
       float4 o;
       o.x = __fdiv_rn(A.x, L);
@@ -355,15 +386,15 @@ decode_attn_kernel(DecArgs a) {
       reinterpret_cast<float4*>(a.out + (static_cast<int64_t>(b) * a.hq + hk * G + h) * D)[c] = o;
     }
   }
-  cluster_sync();      // keep every CTA's shared memory alive until rank 0 has read it
+  cluster_sync();      // keep every CTA's shared memory alive until all ranks have read it
 }
 
 template <int D, int G>
 int launch_dec(const DecArgs& a, int64_t B, int cluster, cudaStream_t stream) {
   constexpr int NST = D == 128 ? 6 : 8;
-  constexpr int GP = G < 8 ? 8 : G;
-  const size_t smem = (2ull * NST * kTK * D + static_cast<size_t>(G) * D + GP * (kTK + 1) + GP +
-                       static_cast<size_t>(G) * (D + 4)) * 4 + NST * 8 + 16;
+  constexpr int CK = (NST / 2) * kTK;
+  const size_t smem = (2ull * NST * kTK * D + static_cast<size_t>(G) * D + G * (CK + 1) +
+                       3 * G + 4 + static_cast<size_t>(G) * (D + 4)) * 4 + NST * 8 + 16;
   auto kern = decode_attn_kernel<D, G, NST>;
   if (smem > 48 * 1024 && set_smem_optin(reinterpret_cast<const void*>(kern), smem) != KSH_OK)
     return KSH_ERR_CUDA;

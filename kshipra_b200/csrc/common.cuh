@@ -97,6 +97,8 @@ inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
 
 int num_sms();
 int set_smem_optin(const void* kernel, size_t bytes);
+// CTAs of `kernel` resident per SM at this block size / dynamic smem (cached).
+int resident_ctas(const void* kernel, int threads, size_t smem);
 
 }  // namespace ksh
 

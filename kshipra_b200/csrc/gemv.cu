@@ -305,8 +305,28 @@ gemv_kernel(LinArgs a, int kt, int prefetch) {
   const int ktv = kt / 4;
   const bool single = keff <= kt;
   const int64_t rb = row_bytes<WK>(a);
-  const int64_t rg0 = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
   const int nv_row = static_cast<int>(keff / E);
+  // This CTA owns the contiguous row groups [g_begin, g_end) (8 rows each,
+  // warp w takes row w of a group); in the multi-tile case one group.
+  const int64_t ngroups = (nrg + kWarps - 1) / kWarps;
+  const int64_t gpc = single ? (ngroups + gridDim.x - 1) / gridDim.x : 1;
+  const int64_t g_begin = static_cast<int64_t>(blockIdx.x) * gpc;
+  const int64_t g_end = g_begin + gpc < ngroups ? g_begin + gpc : ngroups;
+  const int64_t rg0 = g_begin * kWarps + warp;
+  // rows of the first half (SwiGLU: gate rows; the up rows follow at +inter)
+  auto prefetch_groups = [&](int64_t ga, int64_t gb, int tid, int nthr) {
+    if (ga >= gb) return;
+    const int64_t r_lo = ga * kWarps;
+    const int64_t r_hi = gb * kWarps < nrg ? gb * kWarps : nrg;
+    const char* base = static_cast<const char*>(a.w) + r_lo * rb;
+    prefetch_range_l2(base, static_cast<size_t>((r_hi - r_lo) * rb), tid, nthr);
+    if constexpr (EPI == EPI_SWIGLU)
+      prefetch_range_l2(base + a.inter * rb, static_cast<size_t>((r_hi - r_lo) * rb), tid, nthr);
+  };
+  // L2 prefetch distance: about kPrefetchBytes of this CTA's rows ahead.
+  constexpr int64_t kPrefetchBytes = 96 * 1024;
+  const int64_t group_bytes = kWarps * rb * (EPI == EPI_SWIGLU ? 2 : 1);
+  const int64_t pf_dist = kPrefetchBytes / group_bytes > 1 ? kPrefetchBytes / group_bytes : 1;
 
   // ---- constant data, safe before the dependency wait ----
   constexpr int kHoist = hoist_count<WK, EPI, MT>();
@@ -323,16 +343,9 @@ gemv_kernel(LinArgs a, int kt, int prefetch) {
       }
     }
   }
-  if (prefetch && (!single || nv_row > 32 * kHoist)) {
-    const int64_t r_lo = static_cast<int64_t>(blockIdx.x) * kWarps;
-    if (r_lo < nrg) {
-      const int64_t nr = nrg - r_lo < kWarps ? nrg - r_lo : kWarps;
-      const char* base = static_cast<const char*>(a.w) + r_lo * rb;
-      prefetch_range_l2(base, static_cast<size_t>(nr * rb), threadIdx.x, kThreads);
-      if constexpr (EPI == EPI_SWIGLU)
-        prefetch_range_l2(base + a.inter * rb, static_cast<size_t>(nr * rb), threadIdx.x,
-                          kThreads);
-    }
+  if (prefetch) {
+    const int64_t ge = g_begin + pf_dist < g_end ? g_begin + pf_dist : g_end;
+    if (ge > g_begin + 1 || nv_row > 32 * kHoist) prefetch_groups(g_begin, ge, threadIdx.x, kThreads);
   }
   grid_dep_wait();
   grid_dep_launch();
@@ -346,7 +359,12 @@ gemv_kernel(LinArgs a, int kt, int prefetch) {
   if (single) {
     stage_x<WK, MT>(a, xs, ktv, 0, static_cast<int>(keff), inv_rms);
     __syncthreads();
-    for (int64_t rg = rg0; rg < nrg; rg += static_cast<int64_t>(gridDim.x) * kWarps) {
+    for (int64_t gi = g_begin; gi < g_end; ++gi) {
+      // keep the L2 prefetch pf_dist groups ahead (warp 0)
+      if (prefetch && warp == 0 && gi + pf_dist < g_end)
+        prefetch_groups(gi + pf_dist, gi + pf_dist + 1, lane, 32);
+      const int64_t rg = gi * kWarps + warp;
+      if (rg >= nrg) break;
       float acc0[MT], acc1[MT];
 #pragma unroll
       for (int mm = 0; mm < MT; ++mm) acc0[mm] = acc1[mm] = 0.0f;
@@ -447,9 +465,9 @@ int launch_t(const LinArgs& a, cudaStream_t stream) {
   }
   const int64_t nrg = EPI == EPI_SWIGLU ? a.inter : a.n;
   int64_t grid = (nrg + kWarps - 1) / kWarps;
-  if (keff <= kt && ARGMAX) {
-    // persistent row loop, at most one resident wave
-    const int per_sm = static_cast<int>(std::min<int64_t>(8, (200 * 1024) / std::max<size_t>(smem, 1)));
+  if (keff <= kt) {
+    // contiguous row blocks per CTA, exactly one resident wave
+    const int per_sm = resident_ctas(reinterpret_cast<const void*>(kern), kThreads, smem);
     grid = std::min(grid, static_cast<int64_t>(num_sms()) * std::max(per_sm, 1));
   }
   if (grid > INT32_MAX) return KSH_ERR_UNSUPPORTED;

@@ -62,6 +62,39 @@ int set_smem_optin(const void* kernel, size_t bytes) {
   return KSH_OK;
 }
 
+int resident_ctas(const void* kernel, int threads, size_t smem) {
+  static std::mutex mu;
+  struct Key {
+    const void* k;
+    int dev, threads;
+    size_t smem;
+    bool operator==(const Key& o) const {
+      return k == o.k && dev == o.dev && threads == o.threads && smem == o.smem;
+    }
+  };
+  struct Hash {
+    size_t operator()(const Key& x) const {
+      return std::hash<const void*>()(x.k) ^ (static_cast<size_t>(x.dev) << 1) ^
+             (static_cast<size_t>(x.threads) << 8) ^ (x.smem << 20);
+    }
+  };
+  static std::unordered_map<Key, int, Hash> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const Key key{kernel, dev, threads, smem};
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, smem) != cudaSuccess) {
+    cudaGetLastError();
+    n = 1;
+  }
+  n = n < 1 ? 1 : n;
+  cache[key] = n;
+  return n;
+}
+
 }  // namespace ksh
 
 extern "C" int ksh_abi_version(void) { return 1; }
