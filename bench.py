@@ -333,6 +333,80 @@ def run_reference(args, wl):
     return res, rank
 
 
+MICRO_SHAPES = [(4096, 6144), (4096, 28672), (14336, 4096)]   # K x N (Llama-3-8B projections)
+MICRO_M = [1, 8, 64, 512, 4096]
+
+
+def micro_case(scheme, m, k, n, dev):
+    """Quantized weight + activations of one microbench point (N(0,1) activations)."""
+    from kshipra_b200.quantization import quantize_int4_per_group, quantize_int8_per_channel
+    g = torch.Generator(device=dev).manual_seed(m * 7 + k + n)
+    w = torch.randn((n, k), generator=g, device=dev) * 0.02
+    qw = quantize_int8_per_channel(w) if scheme == "int8" else quantize_int4_per_group(w, 128)
+    del w
+    x = torch.randn((m, k), generator=g, device=dev)
+    y = torch.empty((m, n), device=dev)
+    return qw, x, y
+
+
+def run_micro(args):
+    """Config: W4/W8 dequant-linear sweep, M in {1,8,64,512,4096} over the 8B shapes."""
+    from kshipra_b200.quantization import Workspace, linear_launch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    hbm, tc_peak, peak_kind = measured_peaks()
+    ws = Workspace()
+    flt = args.micro_filter.split(",") if args.micro_filter else None
+    results = []
+    for scheme in ("int4", "int8"):
+        for (k, n) in MICRO_SHAPES:
+            for m in MICRO_M:
+                tag = f"{scheme}:{m}:{k}x{n}"
+                if flt and tag not in flt:
+                    continue
+                qw, x, y = micro_case(scheme, m, k, n, dev)
+                run = lambda: linear_launch(x, qw, None, None, y, ws=ws)
+                for _ in range(3):
+                    run()
+                torch.cuda.synchronize()
+                if args.profile:
+                    torch.cuda.cudart().cudaProfilerStart()
+                    run()
+                    torch.cuda.synchronize()
+                    torch.cuda.cudart().cudaProfilerStop()
+                    continue
+                reps = 20 if m <= 64 else 5
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(reps):
+                    run()
+                e1.record()
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / reps
+                wbytes = qw.storage_bytes()
+                nbytes = wbytes + m * k * 4 + m * n * 4
+                flops = 2.0 * m * n * k
+                results.append({"scheme": scheme, "m": m, "k": k, "n": n, "us": us,
+                                "gb_s": nbytes / us / 1e3, "hbm_frac": nbytes / us / 1e3 / hbm,
+                                "tflop_s": flops / us / 1e6,
+                                "tensor_frac": flops / us / 1e6 / tc_peak})
+                del qw, x, y
+    if args.profile:
+        print(json.dumps({"profile": "micro", "filter": args.micro_filter}))
+        return
+    gemv4 = [r for r in results if r["scheme"] == "int4" and r["m"] == 1]
+    head = sum(r["hbm_frac"] for r in gemv4) / max(len(gemv4), 1)
+    res = dict(metric="INT4 decode GEMV (M=1) fraction of measured HBM peak, 8B shapes",
+               value=head, unit="fraction", n_gpus=1, steps=1, warmup=3, ms_per_step=None,
+               higher_is_better=True, scaling="none", vs_baseline=None,
+               dtype="fp32 act / int4|int8 weights", data="synthetic",
+               config={"workload": "micro", "shapes_KxN": MICRO_SHAPES, "m": MICRO_M,
+                       "l2": "weights 12.6-117 MB per point; timed back to back"},
+               peaks={"hbm_gbs": hbm, "tensor_tflops": tc_peak, "kind": peak_kind},
+               sweep=results)
+    print(json.dumps(res))
+
+
 def run_profile(args, wl):
     """One request (chunked prefill + decode graph replays) between
     cudaProfilerStart/Stop, after a warm-up, for ncu --profile-from-start off."""
@@ -349,6 +423,35 @@ def run_profile(args, wl):
     for _ in range(2):
         km.generate(prompt, wl["new"], block_size=wl["block"], prefill_chunk=wl["chunk"])
     torch.cuda.synchronize()
+    if args.trace:
+        # CUPTI activity trace of one request (in-graph kernel durations and
+        # the idle gaps between them, which ncu's serialised replay hides).
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            km.generate(prompt, wl["new"], block_size=wl["block"], prefill_chunk=wl["chunk"])
+            torch.cuda.synchronize()
+        evs = [e for e in prof.events() if e.device_type.name == "CUDA" and e.name]
+        evs.sort(key=lambda e: e.time_range.start)
+        # With programmatic dependent launch a kernel starts early and waits,
+        # so its raw duration overlaps its predecessor.  Attribute to each
+        # kernel the time it adds to the critical path: end - previous end.
+        evs.sort(key=lambda e: e.time_range.end)
+        agg = {}
+        busy = 0.0
+        prev_end = evs[0].time_range.start if evs else 0
+        for e in evs:
+            d = e.time_range.end - max(prev_end, e.time_range.start)
+            prev_end = max(prev_end, e.time_range.end)
+            k = e.name.replace("void ", "").replace("ksh::(anonymous namespace)::", "")
+            k = k.split("(")[0][:60]
+            c, t = agg.get(k, (0, 0.0))
+            agg[k] = (c + 1, t + d)
+            busy += d
+        span = evs[-1].time_range.end - evs[0].time_range.start if evs else 0
+        print(json.dumps({"trace": args.workload, "span_us": span, "busy_us": busy,
+                          "kernels": {k: {"n": c, "total_us": t, "avg_us": t / c}
+                                      for k, (c, t) in sorted(agg.items(), key=lambda x: -x[1][1])}}))
+        return
     torch.cuda.cudart().cudaProfilerStart()
     toks = km.generate(prompt, wl["new"], block_size=wl["block"], prefill_chunk=wl["chunk"])
     torch.cuda.synchronize()
@@ -362,11 +465,18 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="qwen05b-int8", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="qwen05b-int8", choices=sorted(WORKLOADS) + ["micro"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="run one request inside cudaProfilerStart/Stop (for ncu)")
+    ap.add_argument("--trace", action="store_true",
+                    help="with --profile: CUPTI trace of one request, per-kernel summary")
+    ap.add_argument("--micro-filter", default=None,
+                    help="micro workload: comma list of scheme:M:KxN points to run")
     args = ap.parse_args()
+    if args.workload == "micro":
+        run_micro(args)
+        return
     wl = WORKLOADS[args.workload]
     if args.profile:
         run_profile(args, wl)

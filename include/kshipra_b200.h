@@ -49,6 +49,9 @@ const char* ksh_status_string(int status);
 int ksh_last_cuda_error(void);
 /* Enable (1) / disable (0) programmatic dependent launch; returns previous. */
 int ksh_set_pdl(int enabled);
+/* Enable (1) / disable (0) the register-resident decode GEMV for small
+ * matrices (disabled: the streaming GEMV serves all M <= 16); returns previous. */
+int ksh_set_gemv_resident(int enabled);
 
 /* ------------------------------------------------------------------------
  * Weight packing.  w: fp32 [n, k] row-major.

@@ -293,7 +293,7 @@ __device__ __forceinline__ void finish_row(const LinArgs& a, int64_t rg, float (
 }
 
 template <int WK, int EPI, int MT, bool ARGMAX>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, (WK == WK_F32 && MT <= 2) ? 3 : 2)
 gemv_kernel(LinArgs a, int kt, int prefetch) {
   constexpr int E = Vec<WK>::E;
   extern __shared__ float4 xs[];
@@ -495,6 +495,8 @@ int64_t gemv_argmax_grid(int64_t n) {
 int launch_gemv(int wk, int epi, const LinArgs& a, cudaStream_t stream) {
   const bool am = a.argmax_out != nullptr;
   if (epi == EPI_SWIGLU && am) return KSH_ERR_UNSUPPORTED;
+  int st = KSH_OK;
+  if (gemv_resident_enabled() && launch_gemv_resident(wk, epi, a, stream, &st)) return st;
   switch (wk * 4 + epi * 2 + (am ? 1 : 0)) {
     case WK_F32 * 4 + 0: return dispatch_m<WK_F32, EPI_STORE, false>(a, stream);
     case WK_F32 * 4 + 1: return dispatch_m<WK_F32, EPI_STORE, true>(a, stream);

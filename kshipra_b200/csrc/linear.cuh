@@ -33,6 +33,11 @@ struct LinArgs {
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
 int launch_gemv(int wk, int epi, const LinArgs& a, cudaStream_t stream);
+// Register-resident decode GEMV for small matrices; false if not applicable.
+bool launch_gemv_resident(int wk, int epi, const LinArgs& a, cudaStream_t stream, int* status);
+// Force the streaming GEMV (tests compare both paths); returns the previous value.
+int set_gemv_resident_enabled(int on);
+bool gemv_resident_enabled();
 int launch_gemm_simt(int wk, int epi, const LinArgs& a, cudaStream_t stream);
 
 }  // namespace ksh

@@ -22,7 +22,11 @@ int env_flag(const char* name, int dflt) {
 }
 std::atomic<int> g_pdl{env_flag("KSH_PDL", 1)};
 std::atomic<int> g_prefetch{env_flag("KSH_L2_PREFETCH", 1)};
+std::atomic<int> g_resident{env_flag("KSH_GEMV_RESIDENT", 1)};
 }  // namespace
+
+int set_gemv_resident_enabled(int on) { return g_resident.exchange(on ? 1 : 0); }
+bool gemv_resident_enabled() { return g_resident.load(std::memory_order_relaxed) != 0; }
 
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 bool prefetch_enabled() { return g_prefetch.load(std::memory_order_relaxed) != 0; }
@@ -102,6 +106,8 @@ extern "C" int ksh_abi_version(void) { return 1; }
 extern "C" int ksh_last_cuda_error(void) { return ksh::g_last_cuda_error.load(); }
 
 extern "C" int ksh_set_pdl(int enabled) { return ksh::g_pdl.exchange(enabled ? 1 : 0); }
+
+extern "C" int ksh_set_gemv_resident(int enabled) { return ksh::set_gemv_resident_enabled(enabled); }
 
 extern "C" const char* ksh_status_string(int status) {
   switch (status) {

@@ -124,17 +124,24 @@ def test_linear_paths_residual_and_swiglu(scheme, m):
         qw = qgu = None
         wf, gf = w.cuda(), wgu.cuda()
         wd, gud = w.numpy(), wgu.numpy()
+    from kshipra_b200 import _lib
     xc = x.cuda()
-    y = res.clone().cuda()
-    linear_launch(xc, qw, wf, bias.cuda(), y, residual=y)
     y64 = x.double().numpy() @ wd.astype(np.float64).T + bias.double().numpy() + res.double().numpy()
-    assert np.abs(y.cpu().numpy() - y64).max() <= 2e-5 * np.abs(y64).max()
-    h = torch.empty((m, I), device="cuda")
-    swiglu_launch(xc, qgu, gf, I, h)
     gu = x.double().numpy() @ gud.astype(np.float64).T
     gg, uu = gu[:, :I], gu[:, I:]
     h64 = gg / (1 + np.exp(-gg)) * uu
-    assert np.abs(h.cpu().numpy() - h64).max() <= 2e-5 * max(np.abs(h64).max(), 1.0)
+    # both decode GEMV variants (register-resident and streaming) for small m
+    for resident in (1, 0):
+        prev = _lib.lib().ksh_set_gemv_resident(resident)
+        try:
+            y = res.clone().cuda()
+            linear_launch(xc, qw, wf, bias.cuda(), y, residual=y)
+            assert np.abs(y.cpu().numpy() - y64).max() <= 2e-5 * np.abs(y64).max(), resident
+            h = torch.empty((m, I), device="cuda")
+            swiglu_launch(xc, qgu, gf, I, h)
+            assert np.abs(h.cpu().numpy() - h64).max() <= 2e-5 * max(np.abs(h64).max(), 1.0), resident
+        finally:
+            _lib.lib().ksh_set_gemv_resident(prev)
 
 
 def _run_attention_case(q, kp, vp, bt, P, C, B):
