@@ -441,16 +441,19 @@ def run_profile(args, wl):
         prev_end = evs[0].time_range.start if evs else 0
         for e in evs:
             d = e.time_range.end - max(prev_end, e.time_range.start)
+            early = prev_end - e.time_range.start        # > 0: started before its predecessor ended
             prev_end = max(prev_end, e.time_range.end)
             k = e.name.replace("void ", "").replace("ksh::(anonymous namespace)::", "")
             k = k.split("(")[0][:60]
-            c, t = agg.get(k, (0, 0.0))
-            agg[k] = (c + 1, t + d)
+            c, t, ea = agg.get(k, (0, 0.0, 0.0))
+            agg[k] = (c + 1, t + d, ea + early)
             busy += d
         span = evs[-1].time_range.end - evs[0].time_range.start if evs else 0
         print(json.dumps({"trace": args.workload, "span_us": span, "busy_us": busy,
-                          "kernels": {k: {"n": c, "total_us": t, "avg_us": t / c}
-                                      for k, (c, t) in sorted(agg.items(), key=lambda x: -x[1][1])}}))
+                          "kernels": {k: {"n": c, "total_us": t, "avg_us": t / c,
+                                          "avg_early_start_us": ea / c}
+                                      for k, (c, t, ea) in sorted(agg.items(),
+                                                                  key=lambda x: -x[1][1])}}))
         return
     torch.cuda.cudart().cudaProfilerStart()
     toks = km.generate(prompt, wl["new"], block_size=wl["block"], prefill_chunk=wl["chunk"])

@@ -38,15 +38,20 @@ namespace {
 
 using namespace tc;
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3;
+constexpr int BM = 128, BN = 128, BK = 64;
+constexpr int NS = 4;                      // TMA stages (x hi/lo + raw weights)
+constexpr int NB = 2;                      // dequantized fp16 B tiles
 constexpr int kThreads = 192;
 constexpr int kMaxSplits = 8;
 constexpr uint32_t kTmemCols = 2 * BN;
-constexpr int A_BYTES = BM * BK * 2;      // one fp16 term
-constexpr int BH_BYTES = BN * BK * 2;     // dequantized fp16 B tile
-constexpr int BRAW_BYTES = BN * BK;       // int8 raw tile (int4 uses half)
-constexpr int STAGE_BYTES = 2 * A_BYTES + BH_BYTES + BRAW_BYTES;
-constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + 256;
+constexpr int A_BYTES = BM * BK * 2;       // one fp16 term
+constexpr int BH_BYTES = BN * BK * 2;      // dequantized fp16 B tile
+constexpr int BRAW_BYTES = BN * BK;        // int8 raw tile (int4 uses half)
+constexpr int STAGE_BYTES = 2 * A_BYTES + BRAW_BYTES;
+constexpr int RING_BYTES = NS * STAGE_BYTES + NB * BH_BYTES;
+constexpr int OUT_LD = BN + 4;             // staging tile row stride (floats)
+static_assert(BM * OUT_LD * 4 <= NS * STAGE_BYTES, "output staging reuses the TMA ring");
+constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(RING_BYTES) + 2 * BN * 4 + BN * 4 + 512;
 
 struct TcArgs {
   const __half* scales;
@@ -60,20 +65,14 @@ struct TcArgs {
   int m, n, inter, kt_total, kt_per_split, kt_per_group, ngroups_row, g;
 };
 
-__device__ __forceinline__ float weight_scale(const TcArgs& a, int wk, int row, int kgroup) {
-  if (row < 0) return 0.0f;
-  if (wk == WK_I8) return __half2float(a.scales[row]);
-  return __half2float(a.scales[static_cast<int64_t>(row) * a.ngroups_row + kgroup]);
-}
-
-// int8 byte -> fp16 bits, exact: 0x6400 | (b ^ 0x80) = 1024 + b + 128.
+// int8 byte pair -> fp16 bits, exact: 0x6400 | (b ^ 0x80) = 1024 + b + 128.
 __device__ __forceinline__ uint32_t i8x2_to_h2(uint32_t w, int byte0) {
   const uint32_t x = w ^ 0x80808080u;
-  const uint32_t sel = static_cast<uint32_t>(byte0) | (4u << 4) | (static_cast<uint32_t>(byte0 + 1) << 8) |
-                       (5u << 12);
+  const uint32_t sel = static_cast<uint32_t>(byte0) | (4u << 4) |
+                       (static_cast<uint32_t>(byte0 + 1) << 8) | (5u << 12);
   const uint32_t h = __byte_perm(x, 0x64646464u, sel);
-  __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __halves2half2(__ushort_as_half(0x6480),
-                                                                             __ushort_as_half(0x6480)));
+  __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h),
+                      __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));
   return *reinterpret_cast<uint32_t*>(&r);
 }
 // two int4 nibbles (k, k+1) -> fp16 bits: 0x6400 | (u ^ 8) = 1024 + q + 8.
@@ -81,10 +80,12 @@ __device__ __forceinline__ uint32_t i4x2_to_h2(uint32_t w, int nib0) {
   const uint32_t lo = ((w >> (4 * nib0)) & 0xFu) ^ 0x8u;
   const uint32_t hi = ((w >> (4 * nib0 + 4)) & 0xFu) ^ 0x8u;
   const uint32_t h = (lo | 0x6400u) | ((hi | 0x6400u) << 16);
-  __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h), __halves2half2(__ushort_as_half(0x6408),
-                                                                             __ushort_as_half(0x6408)));
+  __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&h),
+                      __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408)));
   return *reinterpret_cast<uint32_t*>(&r);
 }
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 template <int WK, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -92,14 +93,17 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
                 const __grid_constant__ CUtensorMap map_w, TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* st_base = smem;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* full = bars;                 // [STAGES] TMA landed
-  uint64_t* bready = bars + STAGES;      // [STAGES] fp16 B tile written
-  uint64_t* empty = bars + 2 * STAGES;   // [STAGES] MMA done with the stage
-  uint64_t* acc_full = bars + 3 * STAGES;      // [2]
-  uint64_t* acc_empty = bars + 3 * STAGES + 2; // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 4);
+  uint8_t* bh_base = smem + NS * STAGE_BYTES;
+  float* sc_s = reinterpret_cast<float*>(smem + RING_BYTES);     // [2][BN] weight scales per group
+  float* bias_s = sc_s + 2 * BN;                                  // [BN]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(bias_s + BN);
+  uint64_t* full = bars;                       // [NS]  TMA landed
+  uint64_t* empty = full + NS;                 // [NS]  MMA done with the stage
+  uint64_t* bready = empty + NS;               // [NB]  fp16 B tile written
+  uint64_t* bfree = bready + NB;               // [NB]  MMA done with the fp16 B tile
+  uint64_t* acc_full = bfree + NB;             // [2]
+  uint64_t* acc_empty = acc_full + 2;          // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
 
@@ -112,16 +116,19 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
   const int ktpg = WK == WK_I4 ? a.kt_per_group : max(ntl, 1);
   const int ngl = (ntl + ktpg - 1) / ktpg;
 
-  auto stage_ah = [&](int s) { return st_base + s * STAGE_BYTES; };
-  auto stage_al = [&](int s) { return st_base + s * STAGE_BYTES + A_BYTES; };
-  auto stage_bh = [&](int s) { return st_base + s * STAGE_BYTES + 2 * A_BYTES; };
-  auto stage_br = [&](int s) { return st_base + s * STAGE_BYTES + 2 * A_BYTES + BH_BYTES; };
+  auto stage_ah = [&](int s) { return smem + s * STAGE_BYTES; };
+  auto stage_al = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES; };
+  auto stage_br = [&](int s) { return smem + s * STAGE_BYTES + 2 * A_BYTES; };
+  auto tile_bh = [&](int b) { return bh_base + b * BH_BYTES; };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&bready[s], 128);
       mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < NB; ++b) {
+      mbar_init(&bready[b], 128);
+      mbar_init(&bfree[b], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -149,8 +156,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
     if (lane == 0) {
       const uint32_t bytes = 2 * A_BYTES + (WK == WK_I8 ? BN * BK : BN * BK / 2);
       for (int i = 0; i < ntl && !*abort_flag; ++i) {
-        const int s = i % STAGES;
-        if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) {
+        const int s = i % NS;
+        if (i >= NS && !mbar_wait(&empty[s], ((i / NS) - 1) & 1)) {
           *abort_flag = 1;
           break;
         }
@@ -172,20 +179,20 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
     if (lane == 0) {
       const uint32_t idesc = idesc_f16_f32(BM, BN);
       for (int i = 0; i < ntl && !*abort_flag; ++i) {
-        const int s = i % STAGES;
+        const int s = i % NS, b = i % NB;
         const int gl = i / ktpg, buf = gl & 1;
         const bool first = (i % ktpg) == 0;
         if (first && gl >= 2 && !mbar_wait(&acc_empty[buf], ((gl >> 1) - 1) & 1)) {
           *abort_flag = 1;
           break;
         }
-        if (!mbar_wait(&bready[s], (i / STAGES) & 1)) {
+        if (!mbar_wait(&bready[b], (i / NB) & 1)) {      // implies full[s] completed
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
         const uint32_t ah = smem_u32(stage_ah(s)), al = smem_u32(stage_al(s)),
-                       bh = smem_u32(stage_bh(s));
+                       bh = smem_u32(tile_bh(b));
         const uint32_t d = tmem + buf * BN;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
@@ -194,6 +201,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
           mma_f16(d, desc_k_sw128(al + kk * 32), bd, idesc, 1u);
         }
         mma_commit(&empty[s]);
+        mma_commit(&bfree[b]);
         if ((i % ktpg) == ktpg - 1 || i == ntl - 1) mma_commit(&acc_full[buf]);
       }
     }
@@ -202,54 +210,72 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
     const int t = threadIdx.x - 64;          // B tile row this thread converts
     const int q = warp & 3;                  // TMEM lane quadrant of this warp
     const int row_local = q * 32 + lane;     // accumulator row (TMEM lane)
+    // weight row feeding accumulator column / B row t
+    const int wrow_t = [&]() -> int {
+      if (EPI == EPI_SWIGLU) {
+        const int c = n_tile * (BN / 2) + (t & (BN / 2 - 1));
+        if (c >= a.inter) return -1;
+        return t < BN / 2 ? c : a.inter + c;
+      }
+      const int r = n_tile * BN + t;
+      return r < a.n ? r : -1;
+    }();
+    if (EPI == EPI_STORE) bias_s[t] = (a.bias && wrow_t >= 0) ? a.bias[wrow_t] : 0.0f;
     float acc[BN];
 #pragma unroll
     for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
-    // Weight row feeding accumulator column j (for scales); -1 if out of range.
-    auto wrow = [&](int j) -> int {
-      if (EPI == EPI_SWIGLU) {
-        const int c = n_tile * (BN / 2) + (j & (BN / 2 - 1));
-        if (c >= a.inter) return -1;
-        return j < BN / 2 ? c : a.inter + c;
-      }
-      const int r = n_tile * BN + j;
-      return r < a.n ? r : -1;
-    };
+
     auto promote = [&](int gl) -> bool {
       const int buf = gl & 1;
+      epi_bar();                              // every thread's scale for group gl is visible
       if (!mbar_wait(&acc_full[buf], (gl >> 1) & 1)) return false;
       tc_fence_after();
-      const int kgroup = WK == WK_I4 ? (kt_begin + gl * ktpg) / ktpg : 0;
+      const float* sc = sc_s + buf * BN;
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         float v[32];
         tmem_ld_32x32b_x32(tmem + buf * BN + c * 32 + (static_cast<uint32_t>(q * 32) << 16), v);
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) acc[c * 32 + j] = fmaf(v[j], weight_scale(a, WK, wrow(c * 32 + j), kgroup), acc[c * 32 + j]);
+        for (int j = 0; j < 32; ++j) acc[c * 32 + j] = fmaf(v[j], sc[c * 32 + j], acc[c * 32 + j]);
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
+      epi_bar();                              // scale slot `buf` may be rewritten after this
       return true;
     };
 
     bool ok = true;
     for (int i = 0; i < ntl && ok; ++i) {
-      const int s = i % STAGES;
-      if (*abort_flag || !mbar_wait(&full[s], (i / STAGES) & 1)) {
+      const int s = i % NS, b = i % NB;
+      const int gl = i / ktpg;
+      if (*abort_flag || !mbar_wait(&full[s], (i / NS) & 1)) {
         ok = false;
         break;
       }
-      // dequantize row t of the raw tile into the 128B-swizzled fp16 tile
-      uint8_t* bh = stage_bh(s);
+      if (i >= NB && !mbar_wait(&bfree[b], ((i / NB) - 1) & 1)) {
+        ok = false;
+        break;
+      }
+      if ((i % ktpg) == 0) {                 // group scale of row t, into slot gl & 1
+        float scv = 0.0f;
+        if (wrow_t >= 0) {
+          if (WK == WK_I8) scv = __half2float(a.scales[wrow_t]);
+          else scv = __half2float(a.scales[static_cast<int64_t>(wrow_t) * a.ngroups_row +
+                                           (kt_begin + gl * ktpg) / ktpg]);
+        }
+        sc_s[(gl & 1) * BN + t] = scv;
+      }
+      // dequantize row t of the raw tile (TMA-swizzled) into the 128B-swizzled fp16 tile
+      uint8_t* dst_row = tile_bh(b) + (t >> 3) * 1024 + (t & 7) * 128;
       const uint32_t rsw = static_cast<uint32_t>(t & 7);
-      uint8_t* dst_row = bh + (t >> 3) * 1024 + (t & 7) * 128;
       if (WK == WK_I8) {
-        const uint4* src = reinterpret_cast<const uint4*>(stage_br(s) + t * BK);
+        // raw rows are 64 B, TMA 64B swizzle: chunk c at c ^ ((t >> 1) & 3)
+        const uint8_t* src = stage_br(s) + t * BK;
+        const uint32_t rs = static_cast<uint32_t>((t >> 1) & 3);
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const int j = (jj + (t >> 1)) & 3;           // rotate: conflict-free reads
-          const uint4 w = src[j];
+        for (int j = 0; j < 4; ++j) {
+          const uint4 w = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(j) ^ rs) << 4));
           uint4 o0, o1;
           o0.x = i8x2_to_h2(w.x, 0); o0.y = i8x2_to_h2(w.x, 2);
           o0.z = i8x2_to_h2(w.y, 0); o0.w = i8x2_to_h2(w.y, 2);
@@ -259,14 +285,15 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
           *reinterpret_cast<uint4*>(dst_row + (((2 * j + 1) ^ rsw) << 4)) = o1;
         }
       } else {
-        const uint4* src = reinterpret_cast<const uint4*>(stage_br(s) + t * (BK / 2));
+        // raw rows are 32 B, TMA 32B swizzle: chunk c at c ^ ((t >> 2) & 1)
+        const uint8_t* src = stage_br(s) + t * (BK / 2);
+        const uint32_t rs = static_cast<uint32_t>((t >> 2) & 1);
 #pragma unroll
-        for (int jj = 0; jj < 2; ++jj) {
-          const int j = (jj + (t >> 2)) & 1;
-          const uint4 w = src[j];
+        for (int j = 0; j < 2; ++j) {
+          const uint4 w = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(j) ^ rs) << 4));
           const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {              // 8 nibbles -> one 16-byte chunk
+          for (int e = 0; e < 4; ++e) {      // 8 nibbles -> one 16-byte chunk
             uint4 o;
             o.x = i4x2_to_h2(ws[e], 0);
             o.y = i4x2_to_h2(ws[e], 2);
@@ -277,11 +304,8 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
         }
       }
       fence_proxy_async_smem();
-      mbar_arrive(&bready[s]);
-      if (WK == WK_I4 && (i % ktpg) == ktpg - 1) {
-        const int gl = i / ktpg;
-        if (gl >= 1 && !promote(gl - 1)) ok = false;
-      }
+      mbar_arrive(&bready[b]);
+      if (WK == WK_I4 && (i % ktpg) == ktpg - 1 && gl >= 1 && !promote(gl - 1)) ok = false;
     }
     if (ok && ntl > 0 && !*abort_flag) ok = promote(ngl - 1);
     if (!ok) {
@@ -289,64 +313,90 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
       raise_flag(a.flags, KSH_FLAG_TIMEOUT);
     }
 
-    // ---------------- output ----------------
-    const int m = m0 + row_local;
-    const float inv = (m < a.m) ? a.inv_row[m] : 0.0f;
-    const int tiles = gridDim.x * gridDim.y;
-    const int tile = m_tile * gridDim.x + n_tile;
-    bool do_final = true;
-    if (gridDim.z > 1) {
-      float* mine = a.part + ((static_cast<int64_t>(split) * tiles + tile) * BM + row_local) * BN;
+    // ---------------- output: stage the tile in shared memory ----------------
+    // The TMA ring is idle now (every stage was consumed by the MMA).
+    float* stile = reinterpret_cast<float*>(smem);            // [BM][OUT_LD]
+    float* rowp = stile + row_local * OUT_LD;
 #pragma unroll
-      for (int j = 0; j < BN; j += 4)
-        *reinterpret_cast<float4*>(mine + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-      __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (t == 0) *last_flag = (atomicAdd(a.counters + tile, 1u) == gridDim.z - 1) ? 1 : 0;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      do_final = *last_flag != 0;
-      if (do_final) {
-        __threadfence();
+    for (int j = 0; j < BN; j += 4)
+      *reinterpret_cast<float4*>(rowp + j) = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+  }
+
+  // ---------------- split-K reduction through distributed shared memory ----------------
+  // The splits of one output tile form a thread-block cluster along z; rank r
+  // sums rows [r * BM / splits, (r + 1) * BM / splits) of every rank's staged
+  // tile in rank order (deterministic) and writes those rows.
+  __syncthreads();
+  const int splits = static_cast<int>(gridDim.z);
+  if (splits > 1) cluster_sync();
+  if (warp >= 2) {
+    const int t = threadIdx.x - 64;
+    float* stile = reinterpret_cast<float*>(smem);
+    const int rows_per = (BM + splits - 1) / splits;
+    const int r_lo = split * rows_per, r_hi = min(BM, r_lo + rows_per);
+    const uint32_t sbase = smem_u32(stile);
+    auto row_sum = [&](int r, int c4) -> float4 {
+      if (splits == 1) return reinterpret_cast<const float4*>(stile + r * OUT_LD)[c4];
+      const uint32_t off = static_cast<uint32_t>((r * OUT_LD + 4 * c4) * 4);
+      float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 v[kMaxSplits];
 #pragma unroll
-        for (int j = 0; j < BN; ++j) acc[j] = 0.0f;
-        for (int sp = 0; sp < static_cast<int>(gridDim.z); ++sp) {
-          const float* p = a.part + ((static_cast<int64_t>(sp) * tiles + tile) * BM + row_local) * BN;
+      for (int sp = 0; sp < kMaxSplits; ++sp)
+        if (sp < splits) v[sp] = ld_cluster_f32x4(map_rank(sbase + off, static_cast<uint32_t>(sp)));
 #pragma unroll
-          for (int j = 0; j < BN; j += 4) {
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(p + j));
-            acc[j] += v.x; acc[j + 1] += v.y; acc[j + 2] += v.z; acc[j + 3] += v.w;
-          }
+      for (int sp = 0; sp < kMaxSplits; ++sp)
+        if (sp < splits) {
+          s4.x += v[sp].x; s4.y += v[sp].y; s4.z += v[sp].z; s4.w += v[sp].w;
         }
-        if (t == 0) a.counters[tile] = 0u;
-      }
-    }
-    if (do_final && m < a.m) {
-      if (EPI == EPI_SWIGLU) {
+      return s4;
+    };
+    if (EPI == EPI_SWIGLU) {
+      // columns [0, 64) gate, [64, 128) up; 16 float4 outputs per row
+      const int oc4 = t & 15, orr = t >> 4;                 // rows r_lo + orr + 8i
+      const int c = n_tile * (BN / 2) + 4 * oc4;
+      for (int r = r_lo + orr; r < r_hi; r += 8) {
+        const int m = m0 + r;
+        if (m >= a.m) continue;
+        const float inv = a.inv_row[m];
+        const float4 gv = row_sum(r, oc4);
+        const float4 uv = row_sum(r, oc4 + BN / 8);
+        float o[4] = {silu_f(gv.x * inv) * (uv.x * inv), silu_f(gv.y * inv) * (uv.y * inv),
+                      silu_f(gv.z * inv) * (uv.z * inv), silu_f(gv.w * inv) * (uv.w * inv)};
         float* yr = a.y + static_cast<int64_t>(m) * a.inter;
-#pragma unroll
-        for (int j = 0; j < BN / 2; ++j) {
-          const int c = n_tile * (BN / 2) + j;
-          if (c < a.inter) {
-            const float gv = acc[j] * inv, uv = acc[BN / 2 + j] * inv;
-            yr[c] = silu_f(gv) * uv;
-          }
+        if (c + 3 < a.inter && (a.inter & 3) == 0) {
+          *reinterpret_cast<float4*>(yr + c) = make_float4(o[0], o[1], o[2], o[3]);
+        } else {
+          for (int e = 0; e < 4; ++e)
+            if (c + e < a.inter) yr[c + e] = o[e];
         }
-      } else {
+      }
+    } else {
+      const int c4 = t & 31, rr0 = t >> 5;                  // float4 column, rows r_lo + rr0 + 4i
+      const int c = n_tile * BN + 4 * c4;
+      const bool vec = (a.n & 3) == 0 && c + 3 < a.n;
+      for (int r = r_lo + rr0; r < r_hi; r += 4) {
+        const int m = m0 + r;
+        if (m >= a.m) continue;
+        const float inv = a.inv_row[m];
+        const float4 v = row_sum(r, c4);
+        float o[4] = {v.x * inv + bias_s[4 * c4], v.y * inv + bias_s[4 * c4 + 1],
+                      v.z * inv + bias_s[4 * c4 + 2], v.w * inv + bias_s[4 * c4 + 3]};
         float* yr = a.y + static_cast<int64_t>(m) * a.n;
-        const float* rr = a.residual ? a.residual + static_cast<int64_t>(m) * a.n : nullptr;
-#pragma unroll
-        for (int j = 0; j < BN; ++j) {
-          const int c = n_tile * BN + j;
-          if (c < a.n) {
-            float v = acc[j] * inv;
-            if (a.bias) v += a.bias[c];
-            if (rr) v = rr[c] + v;
-            yr[c] = v;
+        const float* rres = a.residual ? a.residual + static_cast<int64_t>(m) * a.n : nullptr;
+        if (vec) {
+          if (rres) {
+            const float4 rv = *reinterpret_cast<const float4*>(rres + c);
+            o[0] = rv.x + o[0]; o[1] = rv.y + o[1]; o[2] = rv.z + o[2]; o[3] = rv.w + o[3];
           }
+          *reinterpret_cast<float4*>(yr + c) = make_float4(o[0], o[1], o[2], o[3]);
+        } else {
+          for (int e = 0; e < 4; ++e)
+            if (c + e < a.n) yr[c + e] = rres ? rres[c + e] + o[e] : o[e];
         }
       }
     }
   }
+  if (splits > 1) cluster_sync();     // every rank's tile stays alive until all have read it
 
   tc_fence_before();
   __syncthreads();
@@ -460,25 +510,19 @@ int max_splits(int64_t m, int64_t n) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, kMaxSplits)));
 }
 
-// Split-K counters sit at a fixed offset (the first kCounterBytes, zeroed
-// once by the caller and left zero by every call) so that calls of different
-// shapes sharing one workspace never see each other's data there.
-constexpr int64_t kCounterBytes = 64 * 1024;
-
 struct WsLayout {
-  int64_t counters, xh, xl, inv, part, total;
+  int64_t xh, xl, inv, total;
 };
 
+// Workspace: the fp16 hi / lo split of x and the per-row factors.  (Split-K
+// partial sums never leave the SMs: they are reduced over the cluster.)
 WsLayout ws_layout(int64_t m, int64_t k, int64_t n_rows) {
+  (void)n_rows;
   WsLayout w = {};
-  const int64_t tiles = ((n_rows + BN - 1) / BN) * ((m + BM - 1) / BM);
-  w.counters = 0;
-  w.xh = kCounterBytes;
+  w.xh = 0;
   w.xl = w.xh + align256(m * k * 2);
   w.inv = w.xl + align256(m * k * 2);
-  w.part = w.inv + align256(m * 4);
-  const int sp = tiles * 4 <= kCounterBytes ? max_splits(m, n_rows) : 1;
-  w.total = w.part + (sp > 1 ? static_cast<int64_t>(sp) * tiles * BM * BN * 4 : 0);
+  w.total = w.inv + align256(m * 4);
   return w;
 }
 
@@ -492,8 +536,7 @@ TcPlan plan(int wk, int64_t m, int64_t keff, int64_t n_rows, int64_t g) {
   p.tiles_m = static_cast<int>((m + BM - 1) / BM);
   p.kt_total = static_cast<int>((keff + BK - 1) / BK);
   p.kt_per_group = wk == WK_I4 ? static_cast<int>(g / BK) : 1;
-  const int64_t tiles = static_cast<int64_t>(p.tiles_n) * p.tiles_m;
-  int splits = tiles * 4 <= kCounterBytes ? max_splits(m, n_rows) : 1;
+  int splits = max_splits(m, n_rows);
   // at least 4 K tiles per split, split boundaries on group boundaries
   splits = std::min(splits, std::max(1, p.kt_total / 4));
   int kps = (p.kt_total + splits - 1) / splits;
@@ -522,11 +565,13 @@ int launch_tc(const LinArgs& a, char* ws, cudaStream_t stream) {
                 CU_TENSOR_MAP_SWIZZLE_128B))
     return KSH_ERR_CUDA;
   const uint32_t box_rows = EPI == EPI_SWIGLU ? BN / 2 : BN;
+  // raw weight tiles: 64-byte (int8) / 32-byte (int4) rows, TMA-swizzled so the
+  // dequantizing threads read them without bank conflicts
   const bool ok = WK == WK_I8
                       ? make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.k, n_rows, a.k, BK,
-                                 box_rows, CU_TENSOR_MAP_SWIZZLE_NONE)
+                                 box_rows, CU_TENSOR_MAP_SWIZZLE_64B)
                       : make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.kp / 2, n_rows,
-                                 a.kp / 2, BK / 2, box_rows, CU_TENSOR_MAP_SWIZZLE_NONE);
+                                 a.kp / 2, BK / 2, box_rows, CU_TENSOR_MAP_SWIZZLE_32B);
   if (!ok) return KSH_ERR_CUDA;
   TcArgs t = {};
   t.scales = a.scales;
@@ -534,8 +579,6 @@ int launch_tc(const LinArgs& a, char* ws, cudaStream_t stream) {
   t.residual = a.residual;
   t.inv_row = inv;
   t.y = a.y;
-  t.part = reinterpret_cast<float*>(ws + L.part);
-  t.counters = reinterpret_cast<uint32_t*>(ws + L.counters);
   t.flags = nullptr;
   t.m = static_cast<int>(a.m);
   t.n = static_cast<int>(a.n);
@@ -549,8 +592,22 @@ int launch_tc(const LinArgs& a, char* ws, cudaStream_t stream) {
   if (set_smem_optin(reinterpret_cast<const void*>(kern), SMEM_BYTES) != KSH_OK) return KSH_ERR_CUDA;
   const unsigned gx = EPI == EPI_SWIGLU ? static_cast<unsigned>((a.inter + BN / 2 - 1) / (BN / 2))
                                         : static_cast<unsigned>(p.tiles_n);
-  return launch(kern, dim3(gx, static_cast<unsigned>(p.tiles_m), static_cast<unsigned>(p.splits)),
-                dim3(kThreads), SMEM_BYTES, stream, mxh, mxl, mw, t);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(gx, static_cast<unsigned>(p.tiles_m), static_cast<unsigned>(p.splits));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;      // the splits of a tile = one cluster
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = static_cast<unsigned>(p.splits);
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mxh, mxl, mw, t);
+  return e == cudaSuccess ? KSH_OK : record_cuda_error(e);
 }
 
 }  // namespace
