@@ -66,26 +66,41 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Staged K / V tiles: 16 rows x D floats as D/32 TMA boxes of 16 rows x 128 B,
+// 128B-swizzled (16-byte chunk c of row r at chunk c ^ (r & 7)).  Float4
+// column d4 of row r:
+template <int D>
+__device__ __forceinline__ int tile_off(int r, int d4) {
+  return (d4 >> 3) * (kTK * 32) + r * 32 + (((d4 & 7) ^ (r & 7)) << 2);
+}
+
 template <int D, int G, int NST>
 __global__ void __launch_bounds__(kThreads)
-decode_attn_kernel(DecArgs a) {
+decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
   constexpr int D4 = D / 4;
-  constexpr int TILE_F = kTK * D;               // floats per K (or V) tile
+  constexpr int TILE_F = kTK * D;               // floats per staged K (or V) tile
   constexpr int CH = NST / 2;                   // tiles per chunk (ring = 2 chunks)
-  constexpr int CK = CH * kTK;                  // keys per chunk
-  constexpr int NPV = (G * D4 + kThreads - 1) / kThreads;   // (head, float4 col) pairs per thread
+  constexpr int CK = CH * kTK;                  // keys per chunk (64 or 128)
+  constexpr int KW = CK / 32;                   // score warps along keys (one key per lane)
+  static_assert(CK % 32 == 0 && KW >= 1 && KW <= kThreads / 32, "score mapping");
+  constexpr int HW = (kThreads / 32) / KW;      // score warps along heads
+  constexpr int GH = (G + HW - 1) / HW;         // heads per score warp
+  constexpr int KGS = kThreads / D4;            // PV key groups
+  constexpr int KPG = CK / KGS;                 // keys per PV group and chunk
   extern __shared__ __align__(128) float4 sm4[];
-  float* sm = reinterpret_cast<float*>(sm4);
-  float* Kt = sm;                               // [NST][kTK][D]
-  float* Vt = Kt + NST * TILE_F;                // [NST][kTK][D]
+  // TMA 128B-swizzled destinations need 1024-byte alignment
+  float* sm = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(sm4) + 1023) & ~uintptr_t(1023));
+  float* Kt = sm;                               // [NST][D/32][kTK][32], swizzled
+  float* Vt = Kt + NST * TILE_F;                // [NST][D/32][kTK][32], swizzled
   float* Qs = Vt + NST * TILE_F;                // [G][D]
   float* Ss = Qs + G * D;                       // [G][CK + 1]
   float* corr_s = Ss + G * (CK + 1);            // [G]
   float* ms = corr_s + G;                       // [G] running max
   float* ls = ms + G;                           // [G] running sum
   // offsets so far: 2*NST*TILE_F + G*D + G*CK + 4G floats, a multiple of 4
-  float* part = ls + G;                         // [G][D + 4]: m, l, pad, pad, acc (16B aligned)
-  uint64_t* full = reinterpret_cast<uint64_t*>(part + G * (D + 4));   // [NST]
+  // [kMaxCluster][G][D + 4]: every rank's (m, l, pad, pad, acc), received by rank 0
+  float* part = ls + G;
+  uint64_t* full = reinterpret_cast<uint64_t*>(part + kMaxCluster * G * (D + 4));   // [NST]
   __shared__ int tile_ok[NST];
   __shared__ float newk[D], newv[D];
 
@@ -108,7 +123,9 @@ decode_attn_kernel(DecArgs a) {
   const int64_t head_rows = a.hkv * a.bs;                         // rows between K and V
   const int32_t* bt = a.block_tables + static_cast<int64_t>(b) * a.max_blocks;
 
-  auto issue = [&](int i) {          // local tile i into stage i % NST (thread 0)
+  // Thread 0 stages local tile i into stage i % NST with TMA (D/32 boxes for K
+  // and for V); an out-of-range block id marks the tile bad instead.
+  auto issue = [&](int i) {
     const int s = i % NST;
     const int t = t_begin + i;
     const int64_t j = (static_cast<int64_t>(t) * kTK) / a.bs;
@@ -120,16 +137,20 @@ decode_attn_kernel(DecArgs a) {
       return;
     }
     tile_ok[s] = 1;
-    const float* kp = a.pool + ((((blk * a.num_layers + a.layer) * 2) * a.hkv + hk) * a.bs + off) * D;
-    const float* vp = kp + head_rows * D;
+    const int krow = static_cast<int>((((blk * a.num_layers + a.layer) * 2) * a.hkv + hk) * a.bs + off);
+    const int vrow = krow + static_cast<int>(head_rows);
     mbar_arrive_expect_tx(&full[s], 2u * TILE_F * 4u);
-    bulk_g2s(Kt + s * TILE_F, kp, TILE_F * 4u, &full[s]);
-    bulk_g2s(Vt + s * TILE_F, vp, TILE_F * 4u, &full[s]);
+#pragma unroll
+    for (int cb = 0; cb < D / 32; ++cb) {
+      tma_load_2d(Kt + s * TILE_F + cb * kTK * 32, &pool_map, &full[s], cb * 32, krow);
+      tma_load_2d(Vt + s * TILE_F + cb * kTK * 32, &pool_map, &full[s], cb * 32, vrow);
+    }
   };
 
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) mbar_init(&full[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_tmap(&pool_map);
     for (int i = 0; i < ntl && i < NST; ++i) issue(i);
   }
   if (tid < G) {
@@ -188,10 +209,13 @@ decode_attn_kernel(DecArgs a) {
     }
   }
 
-  // ---- chunks of CH tiles ----
-  float4 acc[NPV];
+  // ---- chunks of CH tiles (CK = 64 keys) ----
+  // PV ownership: float4 column c4 over the KPG keys kg*KPG .. of each chunk,
+  // all G heads; partial sums stay per thread until the end.
+  const int c4 = tid % D4, kg = tid / D4;
+  float4 acc[G];
 #pragma unroll
-  for (int u = 0; u < NPV; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int h = 0; h < G; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
   bool timed_out = false, bad_block = false;
 
   for (int c0 = 0; c0 < ntl && !timed_out; c0 += CH) {
@@ -205,34 +229,44 @@ decode_attn_kernel(DecArgs a) {
       const int i = ntl - 1, s = i % NST;
       const int rr = static_cast<int>(p) - (t_begin + i) * kTK;
       for (int j = tid; j < D; j += kThreads) {
-        Kt[s * TILE_F + rr * D + j] = newk[j];
-        Vt[s * TILE_F + rr * D + j] = newv[j];
+        Kt[s * TILE_F + tile_off<D>(rr, j >> 2) + (j & 3)] = newk[j];
+        Vt[s * TILE_F + tile_off<D>(rr, j >> 2) + (j & 3)] = newv[j];
       }
       __syncthreads();
     }
     const int kbase = (t_begin + c0) * kTK;    // absolute position of chunk key 0
     const int nk = nt * kTK;
-    // scores S[h][j] = (q_h . k_j) * scale, -inf beyond the causal bound
-    for (int idx = tid; idx < G * CK; idx += kThreads) {
-      const int h = idx / CK, j = idx - h * CK;
-      float sc = -INFINITY;
-      const int s = (c0 + j / kTK) % NST;
-      if (j < nk && kbase + j < total_c && tile_ok[s]) {
-        const float* kr = Kt + s * TILE_F + (j % kTK) * D;
-        float dot = 0.0f;
+    // scores: warp (kh, hh): lane -> key kh*32 + lane, heads hh*GH ..; q read as broadcast
+    {
+      const int kh = warp % KW, hh = warp / KW;
+      const int j = kh * 32 + lane;
+      const int s = (c0 + (j >> 4)) % NST;
+      const bool valid = j < nk && kbase + j < total_c && tile_ok[s];
+      const float* kt = Kt + s * TILE_F;
+      const int r = j & (kTK - 1);
+      float dot[GH];
 #pragma unroll
-        for (int cc = 0; cc < D4; ++cc) {
-          const int c = (cc + j) & (D4 - 1);
-          const float4 qv = reinterpret_cast<const float4*>(Qs + h * D)[c];
-          const float4 kv = reinterpret_cast<const float4*>(kr)[c];
-          dot = fmaf(qv.x, kv.x, dot);
-          dot = fmaf(qv.y, kv.y, dot);
-          dot = fmaf(qv.z, kv.z, dot);
-          dot = fmaf(qv.w, kv.w, dot);
+      for (int u = 0; u < GH; ++u) dot[u] = 0.0f;
+#pragma unroll
+      for (int d4 = 0; d4 < D4; ++d4) {
+        const float4 kv = *reinterpret_cast<const float4*>(kt + tile_off<D>(r, d4));
+#pragma unroll
+        for (int u = 0; u < GH; ++u) {
+          const int h = hh * GH + u;
+          if (h < G) {
+            const float4 qv = reinterpret_cast<const float4*>(Qs + h * D)[d4];
+            dot[u] = fmaf(qv.x, kv.x, dot[u]);
+            dot[u] = fmaf(qv.y, kv.y, dot[u]);
+            dot[u] = fmaf(qv.z, kv.z, dot[u]);
+            dot[u] = fmaf(qv.w, kv.w, dot[u]);
+          }
         }
-        sc = dot * a.scale;
       }
-      Ss[h * (CK + 1) + j] = sc;
+#pragma unroll
+      for (int u = 0; u < GH; ++u) {
+        const int h = hh * GH + u;
+        if (h < G) Ss[h * (CK + 1) + j] = valid ? dot[u] * a.scale : -INFINITY;
+      }
     }
     __syncthreads();
     // online softmax merge, one warp per head
@@ -259,31 +293,30 @@ decode_attn_kernel(DecArgs a) {
       }
     }
     __syncthreads();
-    // acc[h][c4] = acc * corr[h] + sum_j p[h][j] V[j][c4]
+    // acc[h][c4] = acc * corr[h] + sum_{j in group} p[h][j] V[j][c4]
 #pragma unroll
-    for (int u = 0; u < NPV; ++u) {
-      const int idx = tid + u * kThreads;
-      if (idx < G * D4) {
-        const int h = idx / D4, c4 = idx - h * D4;
-        const float* prow = Ss + h * (CK + 1);
-        float4 pv = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int t = 0; t < nt; ++t) {
-          const float* vt = Vt + ((c0 + t) % NST) * TILE_F;
+    for (int h = 0; h < G; ++h) {
+      const float crr = corr_s[h];
+      acc[h].x *= crr;
+      acc[h].y *= crr;
+      acc[h].z *= crr;
+      acc[h].w *= crr;
+    }
+#pragma unroll 4
+    for (int jj = 0; jj < KPG; ++jj) {
+      const int j = kg * KPG + jj;
+      if (j < nk) {
+        const int s = (c0 + (j >> 4)) % NST;
+        const float4 v =
+            *reinterpret_cast<const float4*>(Vt + s * TILE_F + tile_off<D>(j & (kTK - 1), c4));
 #pragma unroll
-          for (int jj = 0; jj < kTK; ++jj) {
-            const float pj = prow[t * kTK + jj];
-            const float4 v = reinterpret_cast<const float4*>(vt + jj * D)[c4];
-            pv.x = fmaf(pj, v.x, pv.x);
-            pv.y = fmaf(pj, v.y, pv.y);
-            pv.z = fmaf(pj, v.z, pv.z);
-            pv.w = fmaf(pj, v.w, pv.w);
-          }
+        for (int h = 0; h < G; ++h) {
+          const float pj = Ss[h * (CK + 1) + j];
+          acc[h].x = fmaf(pj, v.x, acc[h].x);
+          acc[h].y = fmaf(pj, v.y, acc[h].y);
+          acc[h].z = fmaf(pj, v.z, acc[h].z);
+          acc[h].w = fmaf(pj, v.w, acc[h].w);
         }
-        const float crr = corr_s[h];
-        acc[u].x = __fadd_rn(__fmul_rn(acc[u].x, crr), pv.x);
-        acc[u].y = __fadd_rn(__fmul_rn(acc[u].y, crr), pv.y);
-        acc[u].z = __fadd_rn(__fmul_rn(acc[u].z, crr), pv.z);
-        acc[u].w = __fadd_rn(__fmul_rn(acc[u].w, crr), pv.w);
       }
     }
     __syncthreads();                           // this chunk's stages are free
@@ -295,74 +328,65 @@ decode_attn_kernel(DecArgs a) {
     if (bad_block) raise_flag(a.flags, KSH_FLAG_BAD_BLOCK);
   }
 
-  // ---- publish this CTA's state; every rank merges a slice of the outputs ----
-  if (tid < G) {
-    part[tid * (D + 4)] = ms[tid];
-    part[tid * (D + 4) + 1] = ls[tid];
-  }
+  // ---- reduce the PV key groups (the K ring is idle now) and send this CTA's
+  // (m, l, acc) to cluster rank 0 with remote shared-memory stores ----
+  float* red = Kt;                              // [KGS][G][D]
 #pragma unroll
-  for (int u = 0; u < NPV; ++u) {
-    const int idx = tid + u * kThreads;
-    if (idx < G * D4) {
-      const int h = idx / D4, c4 = idx - h * D4;
-      reinterpret_cast<float4*>(part + h * (D + 4) + 4)[c4] = acc[u];
-    }
-  }
+  for (int h = 0; h < G; ++h)
+    reinterpret_cast<float4*>(red + (kg * G + h) * D)[c4] = acc[h];
   __syncthreads();
-  cluster_sync();
-  {
-    const uint32_t base = smem_u32(part);
-    const int per_rank = (G * D4 + static_cast<int>(csize) - 1) / static_cast<int>(csize);
-    for (int w = static_cast<int>(rank) * per_rank + tid;
-         w < min((static_cast<int>(rank) + 1) * per_rank, G * D4); w += kThreads) {
-      const int h = w / D4, c = w - h * D4;
-      const uint32_t off = static_cast<uint32_t>(h * (D + 4)) * 4u;
-      float mr[kMaxCluster], lr[kMaxCluster];
-      float4 ar[kMaxCluster];
-#pragma unroll
-      for (int r = 0; r < kMaxCluster; ++r) {
-        if (r < static_cast<int>(csize)) {
-          const uint32_t pb = map_rank(base + off, static_cast<uint32_t>(r));
-          mr[r] = ld_cluster_f32(pb);
-          lr[r] = ld_cluster_f32(pb + 4);
-          ar[r] = ld_cluster_f32x4(pb + 16u + static_cast<uint32_t>(c) * 16u);
-        }
-      }
-      float M = -INFINITY;
-#pragma unroll
-      for (int r = 0; r < kMaxCluster; ++r)
-        if (r < static_cast<int>(csize)) M = fmaxf(M, mr[r]);
-      const float Ms = isinf(M) ? 0.0f : M;
-      float L = 0.0f;
-      float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-      for (int r = 0; r < kMaxCluster; ++r) {
-        if (r < static_cast<int>(csize)) {
-          const float wgt = expf(mr[r] - Ms);
-          L = fmaf(lr[r], wgt, L);
-          A.x = fmaf(ar[r].x, wgt, A.x);
-          A.y = fmaf(ar[r].y, wgt, A.y);
-          A.z = fmaf(ar[r].z, wgt, A.z);
-          A.w = fmaf(ar[r].w, wgt, A.w);
-        }
-      }
-      float4 o;
-      o.x = __fdiv_rn(A.x, L);
-      o.y = __fdiv_rn(A.y, L);
-      o.z = __fdiv_rn(A.z, L);
-      o.w = __fdiv_rn(A.w, L);
-      reinterpret_cast<float4*>(a.out + (static_cast<int64_t>(b) * a.hq + hk * G + h) * D)[c] = o;
+  const uint32_t slot0 = smem_u32(part + static_cast<int>(rank) * G * (D + 4));
+  const uint32_t dst = csize > 1 ? map_rank(slot0, 0u) : slot0;
+  for (int w = tid; w < G * D4; w += kThreads) {
+    const int h = w / D4, c = w - h * D4;
+    float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int g2 = 0; g2 < KGS; ++g2) {
+      const float4 v = reinterpret_cast<const float4*>(red + (g2 * G + h) * D)[c];
+      s4.x += v.x; s4.y += v.y; s4.z += v.z; s4.w += v.w;
     }
+    st_cluster_f32x4(dst + static_cast<uint32_t>((h * (D + 4) + 4 + 4 * c) * 4), s4);
   }
-  cluster_sync();      // keep every CTA's shared memory alive until all ranks have read it
+  if (tid < G) {
+    st_cluster_f32(dst + static_cast<uint32_t>(tid * (D + 4) * 4), ms[tid]);
+    st_cluster_f32(dst + static_cast<uint32_t>((tid * (D + 4) + 1) * 4), ls[tid]);
+  }
+  if (csize > 1) cluster_sync();              // all ranks' states have landed in rank 0
+  else __syncthreads();
+  if (rank != 0) return;
+  for (int w = tid; w < G * D4; w += kThreads) {
+    const int h = w / D4, c = w - h * D4;
+    float M = -INFINITY;
+    for (uint32_t r = 0; r < csize; ++r) M = fmaxf(M, part[(r * G + h) * (D + 4)]);
+    const float Ms = isinf(M) ? 0.0f : M;
+    float L = 0.0f;
+    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t r = 0; r < csize; ++r) {
+      const float* pr_ = part + (r * G + h) * (D + 4);
+      const float wgt = expf(pr_[0] - Ms);
+      L = fmaf(pr_[1], wgt, L);
+      const float4 ar = reinterpret_cast<const float4*>(pr_ + 4)[c];
+      A.x = fmaf(ar.x, wgt, A.x);
+      A.y = fmaf(ar.y, wgt, A.y);
+      A.z = fmaf(ar.z, wgt, A.z);
+      A.w = fmaf(ar.w, wgt, A.w);
+    }
+    float4 o;
+    o.x = __fdiv_rn(A.x, L);
+    o.y = __fdiv_rn(A.y, L);
+    o.z = __fdiv_rn(A.z, L);
+    o.w = __fdiv_rn(A.w, L);
+    reinterpret_cast<float4*>(a.out + (static_cast<int64_t>(b) * a.hq + hk * G + h) * D)[c] = o;
+  }
 }
 
 template <int D, int G>
-int launch_dec(const DecArgs& a, int64_t B, int cluster, cudaStream_t stream) {
-  constexpr int NST = D == 128 ? 6 : 8;
+int launch_dec(const CUtensorMap& map, const DecArgs& a, int64_t B, int cluster,
+               cudaStream_t stream) {
+  constexpr int NST = D == 64 ? 16 : 8;           // two chunks of 128 / 64 keys
   constexpr int CK = (NST / 2) * kTK;
   const size_t smem = (2ull * NST * kTK * D + static_cast<size_t>(G) * D + G * (CK + 1) +
-                       3 * G + 4 + static_cast<size_t>(G) * (D + 4)) * 4 + NST * 8 + 16;
+                       3 * G + static_cast<size_t>(kMaxCluster) * G * (D + 4)) * 4 + NST * 8 +
+                      1024;
   auto kern = decode_attn_kernel<D, G, NST>;
   if (smem > 48 * 1024 && set_smem_optin(reinterpret_cast<const void*>(kern), smem) != KSH_OK)
     return KSH_ERR_CUDA;
@@ -380,7 +404,7 @@ int launch_dec(const DecArgs& a, int64_t B, int cluster, cudaStream_t stream) {
   attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, map, a);
   return e == cudaSuccess ? KSH_OK : record_cuda_error(e);
 }
 
@@ -437,8 +461,16 @@ extern "C" int ksh_decode_attention(const float* qkv, int64_t batch, int64_t hq,
   a.scale = static_cast<float>(1.0 / sqrt(static_cast<double>(d)));
   const int cl = decode_attention_cluster(batch, hkv, max_total_len);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // the pool as a 2-D tensor of token rows (D floats each) for TMA
+  const int64_t rows = num_blocks * num_layers * 2 * hkv * block_size;
+  if (rows >= (int64_t(1) << 31)) return KSH_ERR_UNSUPPORTED;
+  CUtensorMap map;
+  if (!make_tensor_map_2d(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, pool, static_cast<uint64_t>(d),
+                          static_cast<uint64_t>(rows), static_cast<uint64_t>(d) * 4, 32, kTK,
+                          CU_TENSOR_MAP_SWIZZLE_128B))
+    return KSH_ERR_UNSUPPORTED;
 #define KSH_DEC(DD, GG) \
-  if (d == DD && g == GG) return launch_dec<DD, GG>(a, batch, cl, st);
+  if (d == DD && g == GG) return launch_dec<DD, GG>(map, a, batch, cl, st);
   KSH_DEC(64, 1) KSH_DEC(64, 2) KSH_DEC(64, 4) KSH_DEC(64, 7) KSH_DEC(64, 8)
   KSH_DEC(128, 1) KSH_DEC(128, 2) KSH_DEC(128, 4) KSH_DEC(128, 8)
 #undef KSH_DEC

@@ -474,33 +474,6 @@ split_x_kernel(const float* __restrict__ x, int64_t k, __half* __restrict__ xh,
 // host side
 // ---------------------------------------------------------------------------
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-bool make_map(CUtensorMap* map, CUtensorMapDataType dt, const void* base, uint64_t inner,
-              uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
-              CUtensorMapSwizzle sw) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t es[2] = {1, 1};
-  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
 
 int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 
@@ -559,18 +532,18 @@ int launch_tc(const LinArgs& a, char* ws, cudaStream_t stream) {
                   xh, xl, inv, a.norm_w, a.norm_eps);
   if (st != KSH_OK) return st;
   CUtensorMap mxh, mxl, mw;
-  if (!make_map(&mxh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, a.k, a.m, a.k * 2, BK, BM,
+  if (!make_tensor_map_2d(&mxh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, a.k, a.m, a.k * 2, BK, BM,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mxl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xl, a.k, a.m, a.k * 2, BK, BM,
+      !make_tensor_map_2d(&mxl, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xl, a.k, a.m, a.k * 2, BK, BM,
                 CU_TENSOR_MAP_SWIZZLE_128B))
     return KSH_ERR_CUDA;
   const uint32_t box_rows = EPI == EPI_SWIGLU ? BN / 2 : BN;
   // raw weight tiles: 64-byte (int8) / 32-byte (int4) rows, TMA-swizzled so the
   // dequantizing threads read them without bank conflicts
   const bool ok = WK == WK_I8
-                      ? make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.k, n_rows, a.k, BK,
+                      ? make_tensor_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.k, n_rows, a.k, BK,
                                  box_rows, CU_TENSOR_MAP_SWIZZLE_64B)
-                      : make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.kp / 2, n_rows,
+                      : make_tensor_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.kp / 2, n_rows,
                                  a.kp / 2, BK / 2, box_rows, CU_TENSOR_MAP_SWIZZLE_32B);
   if (!ok) return KSH_ERR_CUDA;
   TcArgs t = {};
@@ -626,7 +599,7 @@ int launch_gemm_tc(int wk, int epi, const LinArgs& a, void* ws, int64_t ws_bytes
   if (wk == WK_I8 && a.k % 16 != 0) return KSH_OK;
   if (wk == WK_I4 && (a.g % BK != 0 || (a.kp / 2) % 16 != 0)) return KSH_OK;
   if (a.k % 8 != 0) return KSH_OK;
-  if (!encode_fn()) return KSH_OK;
+  if (!tensor_map_encoder_available()) return KSH_OK;
   const WsLayout L = ws_layout(a.m, a.k, a.n);
   if (!ws || ws_bytes < L.total || (reinterpret_cast<uintptr_t>(ws) & 255) != 0) return KSH_OK;
   *taken = true;

@@ -8,7 +8,9 @@
 #include <unordered_map>
 #include <utility>
 
-#include "common.cuh"
+#include <cudaTypedefs.h>
+
+#include "tc_common.cuh"
 
 namespace ksh {
 
@@ -64,6 +66,39 @@ int set_smem_optin(const void* kernel, size_t bytes) {
   if (e != cudaSuccess) return record_cuda_error(e);
   cur = bytes;
   return KSH_OK;
+}
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+}  // namespace
+
+bool tensor_map_encoder_available() { return encode_fn() != nullptr; }
+
+bool make_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
+                        uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
+                        uint32_t box_outer, CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
 }
 
 int resident_ctas(const void* kernel, int threads, size_t smem) {

@@ -7,6 +7,14 @@
 #include "common.cuh"
 
 namespace ksh {
+
+// Host: 2-D tiled tensor map (rows of `inner` elements, `row_bytes` apart),
+// through the driver entry point (no link-time dependency on libcuda).
+bool tensor_map_encoder_available();
+bool make_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
+                        uint64_t inner, uint64_t outer, uint64_t row_bytes, uint32_t box_inner,
+                        uint32_t box_outer, CUtensorMapSwizzle sw);
+
 namespace tc {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -82,6 +90,15 @@ __device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
                : "r"(addr)
                : "memory");
   return v;
+}
+
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_f32x4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "f"(v.x), "f"(v.y),
+               "f"(v.z), "f"(v.w)
+               : "memory");
 }
 
 // ---- TMA ----
