@@ -307,9 +307,9 @@ gemv_kernel(LinArgs a, int kt, int prefetch) {
   const int64_t rb = row_bytes<WK>(a);
   const int nv_row = static_cast<int>(keff / E);
   // This CTA owns the contiguous row groups [g_begin, g_end) (8 rows each,
-  // warp w takes row w of a group); in the multi-tile case one group.
+  // warp w takes row w of a group).
   const int64_t ngroups = (nrg + kWarps - 1) / kWarps;
-  const int64_t gpc = single ? (ngroups + gridDim.x - 1) / gridDim.x : 1;
+  const int64_t gpc = (ngroups + gridDim.x - 1) / gridDim.x;
   const int64_t g_begin = static_cast<int64_t>(blockIdx.x) * gpc;
   const int64_t g_end = g_begin + gpc < ngroups ? g_begin + gpc : ngroups;
   const int64_t rg0 = g_begin * kWarps + warp;
@@ -382,20 +382,27 @@ gemv_kernel(LinArgs a, int kt, int prefetch) {
       finish_row<WK, EPI, MT, ARGMAX>(a, rg, acc0, acc1, best);
     }
   } else {
-    const int64_t rg = rg0;
-    const bool active = rg < nrg;
-    const int64_t r1 = EPI == EPI_SWIGLU ? rg + a.inter : rg;
-    float acc0[MT], acc1[MT];
+    // x does not fit shared memory at once: every group streams the x tiles
+    // (the loop bounds are CTA-uniform; the barriers inside are reached by
+    // all threads).
+    for (int64_t gi = g_begin; gi < g_end; ++gi) {
+      if (prefetch && warp == 0 && gi + pf_dist < g_end)
+        prefetch_groups(gi + pf_dist, gi + pf_dist + 1, lane, 32);
+      const int64_t rg = gi * kWarps + warp;
+      const bool active = rg < nrg;
+      const int64_t r1 = EPI == EPI_SWIGLU ? rg + a.inter : rg;
+      float acc0[MT], acc1[MT];
 #pragma unroll
-    for (int mm = 0; mm < MT; ++mm) acc0[mm] = acc1[mm] = 0.0f;
-    for (int64_t k0 = 0; k0 < keff; k0 += kt) {
-      const int kl = static_cast<int>(keff - k0 < kt ? keff - k0 : kt);
-      __syncthreads();
-      stage_x<WK, MT>(a, xs, ktv, k0, kl, inv_rms);
-      __syncthreads();
-      if (active) accumulate<WK, EPI, MT>(a, xs, ktv, rg, r1, k0, kl, 0, acc0, acc1);
+      for (int mm = 0; mm < MT; ++mm) acc0[mm] = acc1[mm] = 0.0f;
+      for (int64_t k0 = 0; k0 < keff; k0 += kt) {
+        const int kl = static_cast<int>(keff - k0 < kt ? keff - k0 : kt);
+        __syncthreads();
+        stage_x<WK, MT>(a, xs, ktv, k0, kl, inv_rms);
+        __syncthreads();
+        if (active) accumulate<WK, EPI, MT>(a, xs, ktv, rg, r1, k0, kl, 0, acc0, acc1);
+      }
+      if (active) finish_row<WK, EPI, MT, ARGMAX>(a, rg, acc0, acc1, best);
     }
-    if (active) finish_row<WK, EPI, MT, ARGMAX>(a, rg, acc0, acc1, best);
   }
 
   if constexpr (ARGMAX) {
@@ -464,12 +471,12 @@ int launch_t(const LinArgs& a, cudaStream_t stream) {
     if (set_smem_optin(reinterpret_cast<const void*>(kern), smem) != KSH_OK) return KSH_ERR_CUDA;
   }
   const int64_t nrg = EPI == EPI_SWIGLU ? a.inter : a.n;
-  int64_t grid = (nrg + kWarps - 1) / kWarps;
-  if (keff <= kt) {
-    // contiguous row blocks per CTA, exactly one resident wave
-    const int per_sm = resident_ctas(reinterpret_cast<const void*>(kern), kThreads, smem);
-    grid = std::min(grid, static_cast<int64_t>(num_sms()) * std::max(per_sm, 1));
-  }
+  // Contiguous row blocks per CTA, exactly one resident wave.  At most 8
+  // CTAs of 256 threads fit an SM, so the grid never exceeds
+  // gemv_argmax_grid(), which sizes the argmax partials.
+  const int per_sm = resident_ctas(reinterpret_cast<const void*>(kern), kThreads, smem);
+  const int64_t grid = std::min((nrg + kWarps - 1) / kWarps,
+                                static_cast<int64_t>(num_sms()) * std::min(std::max(per_sm, 1), 8));
   if (grid > INT32_MAX) return KSH_ERR_UNSUPPORTED;
   return launch(kern, dim3(static_cast<unsigned>(grid)), dim3(kThreads), smem, stream, a,
                 static_cast<int>(kt), prefetch_enabled() ? 1 : 0);

@@ -282,6 +282,39 @@ def test_lm_head_argmax_first_index():
             assert tok2.cpu().tolist() == tok.cpu().tolist()
 
 
+@pytest.mark.parametrize("m,H,V", [(8, 4096, 128256), (16, 2048, 32000), (5, 4096, 1000)])
+def test_lm_head_argmax_tiled_x_stays_in_workspace(m, H, V):
+    """Hidden sizes whose staged activations span several shared-memory tiles
+    (Llama-3-8B lm_head at batch 5-16): logits, first-index argmax, and no
+    write past the workspace the size query asked for."""
+    from kshipra_b200 import _lib
+    gen = torch.Generator().manual_seed(m + H + V)
+    w = torch.randn((V, H), generator=gen) * 0.02
+    w[V // 3] = w[V - 5]
+    x = torch.randn((m, H), generator=gen)
+    x[0] = w[V - 5] * 50
+    nw = 1.0 + 0.1 * torch.randn(H, generator=gen)
+    wc, xc, nc = w.cuda(), x.cuda(), nw.cuda()
+    need = int(_lib.lib().ksh_lm_head_workspace_size(m, V))
+    guard = 1 << 20
+    ws = torch.zeros(need + guard, dtype=torch.uint8, device="cuda")
+    ws[need:] = 0xAB
+    logits = torch.empty((m, V), device="cuda")
+    tok = torch.empty(m, dtype=torch.int64, device="cuda")
+    for _ in range(2):
+        _lib.call("ksh_lm_head_argmax", xc.data_ptr(), m, H, nc.data_ptr(), 1e-6, wc.data_ptr(),
+                  V, logits.data_ptr(), tok.data_ptr(), ws.data_ptr(), need, _lib.stream_ptr())
+        torch.cuda.synchronize()
+        assert bool((ws[need:] == 0xAB).all())
+        xd = x.double()
+        xn = xd * torch.rsqrt(xd.pow(2).mean(-1, keepdim=True) + 1e-6) * nw.double()
+        ref = xn @ w.double().T
+        lg = logits.cpu()
+        assert float((lg.double() - ref).abs().max()) <= 1e-5 * float(ref.abs().max())
+        assert tok.cpu().tolist() == torch.argmax(lg, dim=1).tolist()
+        assert int(tok[0]) == V // 3
+
+
 @pytest.mark.parametrize("scheme", ["int8", "int4"])
 @pytest.mark.parametrize("m,k,n", [(128, 896, 1152), (512, 4864, 896), (130, 896, 9728),
                                    (2048, 4096, 512)])
