@@ -33,6 +33,7 @@ extern "C" {
 #define KSH_ERR_CUDA        -3   /* launch failed; see ksh_last_cuda_error() */
 #define KSH_ERR_UNSUPPORTED -4   /* shape outside what the kernels handle */
 #define KSH_ERR_WORKSPACE   -5   /* workspace missing or too small */
+#define KSH_ERR_TOO_LARGE   -6   /* size beyond a fixed scratch array's capacity */
 
 /* ---- device status-word bits ---- */
 #define KSH_FLAG_NONFINITE     1   /* weight holds NaN/Inf (QuantizationError) */
@@ -189,6 +190,20 @@ int ksh_lm_head_argmax(const float* x, int64_t m, int64_t hidden, const float* n
                        float norm_eps, const float* w,
                        int64_t vocab, float* logits, int64_t* tokens, void* workspace,
                        int64_t workspace_bytes, void* stream);
+/* The same lm_head + greedy argmax (fused GEMV path only) for callers that
+ * cannot allocate device memory: an FFI binding handed only device pointers
+ * by a host runtime whose allocator it cannot reach, or a latency-critical
+ * loop that must not call cudaMalloc (it can synchronize the device).  No
+ * counterpart in the reference.
+ * Scratch is a fixed 256 KiB device array per GPU (its size:
+ * ksh_lm_head_argmax_noalloc_max_bytes()); m <= 16 and vocabularies whose
+ * partials fit it, else KSH_ERR_TOO_LARGE.  The first call on a device looks
+ * up the array's address (make it before any stream capture).  All calls
+ * share the array: calls that overlap on the GPU race.  Allocates nothing. */
+int64_t ksh_lm_head_argmax_noalloc_max_bytes(void);
+int ksh_lm_head_argmax_noalloc(const float* x, int64_t m, int64_t hidden, const float* norm_w,
+                               float norm_eps, const float* w, int64_t vocab, float* logits,
+                               int64_t* tokens, void* stream);
 /* Row-wise argmax of materialised logits [m, vocab]. */
 int ksh_argmax_rows(const float* logits, int64_t m, int64_t vocab, int64_t* out,
                     void* stream);

@@ -50,6 +50,8 @@ SIGNATURES = {
                                    I64, P, I64, I64, P, P, P]),
     "ksh_lm_head_workspace_size": (I64, [I64, I64]),
     "ksh_lm_head_argmax": (I32, [P, I64, I64, P, F32, P, I64, P, P, P, I64, P]),
+    "ksh_lm_head_argmax_noalloc_max_bytes": (I64, []),
+    "ksh_lm_head_argmax_noalloc": (I32, [P, I64, I64, P, F32, P, I64, P, P, P]),
     "ksh_argmax_rows": (I32, [P, I64, I64, P, P]),
     "ksh_decode_advance": (I32, [P, I64, P, P, P, P, P, I64, I64, P, I64, P, P, P]),
 }

@@ -152,6 +152,7 @@ extern "C" const char* ksh_status_string(int status) {
     case KSH_ERR_CUDA: return "CUDA launch failed";
     case KSH_ERR_UNSUPPORTED: return "shape not supported by the kernels";
     case KSH_ERR_WORKSPACE: return "workspace missing or too small";
+    case KSH_ERR_TOO_LARGE: return "size exceeds the fixed scratch array of this entry point";
     default: return "unknown status";
   }
 }
