@@ -4,7 +4,8 @@
 into an object under ``kshipra_b200/_build/`` and links them into
 ``kshipra_b200/libkshipra_b200.so`` with a static CUDA runtime, so the library
 only needs the driver at load time.  Rebuilds when any source or header is
-newer than the library.
+newer than the library; only objects whose source (or a shared header) changed
+are recompiled.
 """
 
 from __future__ import annotations
@@ -51,8 +52,17 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(p) <= t for p in _deps())
 
 
-def _compile(src: str, verbose: bool) -> str:
+def _headers():
+    return (glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h"))
+            + glob.glob(os.path.join(INCLUDE, "*.h")) + [os.path.abspath(__file__)])
+
+
+def _compile(src: str, verbose: bool, force: bool = False) -> str:
     obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
+    # An object is stale when its source or any shared header is newer.
+    if (not force and not verbose and os.path.exists(obj)
+            and all(os.path.getmtime(p) <= os.path.getmtime(obj) for p in [src, *_headers()])):
+        return obj
     cmd = [nvcc(), *ARCH, *FLAGS, "-c", src, "-o", obj]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
@@ -70,7 +80,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     srcs = _sources()
     with cf.ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 4)) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
+        objs = list(ex.map(lambda s: _compile(s, verbose, force), srcs))
     tmp = LIB + ".tmp"
     cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs]
     r = subprocess.run(cmd, capture_output=True, text=True)
