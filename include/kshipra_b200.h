@@ -53,6 +53,12 @@ int ksh_set_pdl(int enabled);
 /* Enable (1) / disable (0) the register-resident decode GEMV for small
  * matrices (disabled: the streaming GEMV serves all M <= 16); returns previous. */
 int ksh_set_gemv_resident(int enabled);
+/* Tensor-core decode path for quantized linears with m <= 16 (swap-AB tcgen05
+ * kernels): 0 off, 1 auto (by scheme, m and matrix size), 2 every eligible
+ * shape, 3 as 2 with INT8 through the fp16-operand kernel (tests).  Returns the
+ * previous mode.  A tuning switch with no counterpart in the reference;
+ * results agree with the CUDA-core path within fp32 rounding. */
+int ksh_set_gemv_tc(int mode);
 
 /* ------------------------------------------------------------------------
  * Weight packing.  w: fp32 [n, k] row-major.

@@ -407,7 +407,7 @@ int launch_attn(const AttnArgs& a, const Plan& p, cudaStream_t stream) {
   const size_t smem = (static_cast<size_t>(RMAX) * D4 + 2 * kTK * D4) * 16 +
                       (static_cast<size_t>(RMAX) * (kTK + 1) + 3 * RMAX) * 4;
   auto kern = paged_attn_kernel<D, RMAX>;
-  if (smem > 48 * 1024 && set_smem_optin(reinterpret_cast<const void*>(kern), smem) != KSH_OK)
+  if (smem > 32 * 1024 && set_smem_optin(reinterpret_cast<const void*>(kern), smem) != KSH_OK)
     return KSH_ERR_CUDA;
   return launch(kern, dim3(static_cast<unsigned>(p.items), static_cast<unsigned>(p.nsplit)),
                 dim3(kThreads), smem, stream, a);

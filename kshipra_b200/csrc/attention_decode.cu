@@ -388,7 +388,7 @@ int launch_dec(const CUtensorMap& map, const DecArgs& a, int64_t B, int cluster,
                        3 * G + static_cast<size_t>(kMaxCluster) * G * (D + 4)) * 4 + NST * 8 +
                       1024;
   auto kern = decode_attn_kernel<D, G, NST>;
-  if (smem > 48 * 1024 && set_smem_optin(reinterpret_cast<const void*>(kern), smem) != KSH_OK)
+  if (smem > 32 * 1024 && set_smem_optin(reinterpret_cast<const void*>(kern), smem) != KSH_OK)
     return KSH_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(cluster), static_cast<unsigned>(B * a.hkv), 1);

@@ -78,13 +78,6 @@ __device__ __forceinline__ uint4 ld_stream(const void* p) {
   return r;
 }
 
-__device__ __forceinline__ float s8f(uint32_t w, int b) {
-  return static_cast<float>(static_cast<int8_t>((w >> (8 * b)) & 0xFFu));
-}
-__device__ __forceinline__ float s4f(uint32_t w, int t) {
-  return static_cast<float>(static_cast<int>(((w >> (4 * t)) & 0xFu) ^ 8u) - 8);
-}
-
 // Dot product of one 16-byte weight vector (local vector index v within the
 // staged tile) with one staged x row.
 template <int WK>
@@ -97,14 +90,14 @@ __device__ __forceinline__ float vec_dot(const uint4& w, int v, const float4* xr
     s = fmaf(__uint_as_float(w.z), x.z, s);
     s = fmaf(__uint_as_float(w.w), x.w, s);
   } else if constexpr (WK == WK_I8) {
-    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+    const uint32_t ws[4] = {bias_i8(w.x), bias_i8(w.y), bias_i8(w.z), bias_i8(w.w)};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float4 x = xr[swz<WK>(4 * v + j)];
-      s = fmaf(s8f(ws[j], 0), x.x, s);
-      s = fmaf(s8f(ws[j], 1), x.y, s);
-      s = fmaf(s8f(ws[j], 2), x.z, s);
-      s = fmaf(s8f(ws[j], 3), x.w, s);
+      s = fmaf(dq_i8(ws[j], 0), x.x, s);
+      s = fmaf(dq_i8(ws[j], 1), x.y, s);
+      s = fmaf(dq_i8(ws[j], 2), x.z, s);
+      s = fmaf(dq_i8(ws[j], 3), x.w, s);
     }
   } else {
     const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
@@ -112,14 +105,15 @@ __device__ __forceinline__ float vec_dot(const uint4& w, int v, const float4* xr
     for (int j = 0; j < 4; ++j) {
       const float4 xa = xr[swz<WK>(8 * v + 2 * j)];
       const float4 xb = xr[swz<WK>(8 * v + 2 * j + 1)];
-      s = fmaf(s4f(ws[j], 0), xa.x, s);
-      s = fmaf(s4f(ws[j], 1), xa.y, s);
-      s = fmaf(s4f(ws[j], 2), xa.z, s);
-      s = fmaf(s4f(ws[j], 3), xa.w, s);
-      s = fmaf(s4f(ws[j], 4), xb.x, s);
-      s = fmaf(s4f(ws[j], 5), xb.y, s);
-      s = fmaf(s4f(ws[j], 6), xb.z, s);
-      s = fmaf(s4f(ws[j], 7), xb.w, s);
+      const uint32_t lo = nib_lo(ws[j]), hi = nib_hi(ws[j]);
+      s = fmaf(dq_i4(lo, 0), xa.x, s);
+      s = fmaf(dq_i4(hi, 0), xa.y, s);
+      s = fmaf(dq_i4(lo, 1), xa.z, s);
+      s = fmaf(dq_i4(hi, 1), xa.w, s);
+      s = fmaf(dq_i4(lo, 2), xb.x, s);
+      s = fmaf(dq_i4(hi, 2), xb.y, s);
+      s = fmaf(dq_i4(lo, 3), xb.z, s);
+      s = fmaf(dq_i4(hi, 3), xb.w, s);
     }
   }
   return s;
@@ -186,8 +180,11 @@ __device__ __forceinline__ void fold_vec(const LinArgs& a, const float4* xs, int
   constexpr int E = Vec<WK>::E;
   float s0 = 1.0f, s1 = 1.0f;
   if constexpr (WK == WK_I4) {
+    // group of this vector's first element; a shift for power-of-two groups
     const int64_t ng = a.kp / a.g;
-    const int64_t grp = (k0 + static_cast<int64_t>(v) * E) / a.g;
+    const uint32_t e0 = static_cast<uint32_t>(k0) + static_cast<uint32_t>(v) * E;
+    const uint32_t g = static_cast<uint32_t>(a.g);
+    const int64_t grp = (g & (g - 1)) == 0 ? (e0 >> (__ffs(g) - 1)) : e0 / g;
     s0 = __half2float(a.scales[r0 * ng + grp]);
     if constexpr (EPI == EPI_SWIGLU) s1 = __half2float(a.scales[r1 * ng + grp]);
   }
@@ -467,7 +464,7 @@ int launch_t(const LinArgs& a, cudaStream_t stream) {
   if (keff <= kt) kt = (keff + 255) / 256 * 256;
   const size_t smem = static_cast<size_t>(MT) * kt * 4;
   auto kern = gemv_kernel<WK, EPI, MT, ARGMAX>;
-  if (smem > 48 * 1024) {
+  if (smem > 32 * 1024) {
     if (set_smem_optin(reinterpret_cast<const void*>(kern), smem) != KSH_OK) return KSH_ERR_CUDA;
   }
   const int64_t nrg = EPI == EPI_SWIGLU ? a.inter : a.n;

@@ -65,25 +65,20 @@ __device__ __forceinline__ float dot_vec(const uint4& w, int v, const float4* xr
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float4 x = xr[swz<WK>(4 * v + j)];
-      s0 = fmaf(static_cast<float>(static_cast<int8_t>(ws[j] & 0xFF)), x.x, s0);
-      s1 = fmaf(static_cast<float>(static_cast<int8_t>((ws[j] >> 8) & 0xFF)), x.y, s1);
-      s0 = fmaf(static_cast<float>(static_cast<int8_t>((ws[j] >> 16) & 0xFF)), x.z, s0);
-      s1 = fmaf(static_cast<float>(static_cast<int8_t>(ws[j] >> 24)), x.w, s1);
+      const uint32_t wb = bias_i8(ws[j]);
+      s0 = fmaf(dq_i8(wb, 0), x.x, s0);
+      s1 = fmaf(dq_i8(wb, 1), x.y, s1);
+      s0 = fmaf(dq_i8(wb, 2), x.z, s0);
+      s1 = fmaf(dq_i8(wb, 3), x.w, s1);
     }
   } else {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float4 xa = xr[swz<WK>(8 * v + 2 * j)];
       const float4 xb = xr[swz<WK>(8 * v + 2 * j + 1)];
-      const float q[8] = {
-          static_cast<float>(static_cast<int>(((ws[j] >> 0) & 0xFu) ^ 8u) - 8),
-          static_cast<float>(static_cast<int>(((ws[j] >> 4) & 0xFu) ^ 8u) - 8),
-          static_cast<float>(static_cast<int>(((ws[j] >> 8) & 0xFu) ^ 8u) - 8),
-          static_cast<float>(static_cast<int>(((ws[j] >> 12) & 0xFu) ^ 8u) - 8),
-          static_cast<float>(static_cast<int>(((ws[j] >> 16) & 0xFu) ^ 8u) - 8),
-          static_cast<float>(static_cast<int>(((ws[j] >> 20) & 0xFu) ^ 8u) - 8),
-          static_cast<float>(static_cast<int>(((ws[j] >> 24) & 0xFu) ^ 8u) - 8),
-          static_cast<float>(static_cast<int>(((ws[j] >> 28) & 0xFu) ^ 8u) - 8)};
+      const uint32_t lo = nib_lo(ws[j]), hi = nib_hi(ws[j]);
+      const float q[8] = {dq_i4(lo, 0), dq_i4(hi, 0), dq_i4(lo, 1), dq_i4(hi, 1),
+                          dq_i4(lo, 2), dq_i4(hi, 2), dq_i4(lo, 3), dq_i4(hi, 3)};
       s0 = fmaf(q[0], xa.x, s0);
       s1 = fmaf(q[1], xa.y, s1);
       s0 = fmaf(q[2], xa.z, s0);
@@ -195,7 +190,11 @@ gemv_resident_kernel(LinArgs a, int rw) {
           const int vec = lane + 32 * v;
           if (vec < nv_row) {
             float sc = 1.0f;
-            if constexpr (WK == WK_I4) sc = __half2float(a.scales[rr * ng + (static_cast<int64_t>(vec) * E) / a.g]);
+            if constexpr (WK == WK_I4) {
+              const uint32_t e0 = static_cast<uint32_t>(vec) * E, g = static_cast<uint32_t>(a.g);
+              sc = __half2float(
+                  a.scales[rr * ng + ((g & (g - 1)) == 0 ? (e0 >> (__ffs(g) - 1)) : e0 / g)]);
+            }
 #pragma unroll
             for (int mm = 0; mm < MT; ++mm) {
               const float d = dot_vec<WK>(w[(j * F + h) * VPL + v], vec, xs + mm * ktv);
@@ -237,7 +236,7 @@ int launch_r(const LinArgs& a, int rw, cudaStream_t stream) {
   const int64_t keff = WK == WK_I4 ? a.kp : a.k;
   const size_t smem = static_cast<size_t>(MT + 1) * keff * 4;
   auto kern = gemv_resident_kernel<WK, EPI, MT, VPL>;
-  if (smem > 48 * 1024 && set_smem_optin(reinterpret_cast<const void*>(kern), smem) != KSH_OK)
+  if (smem > 32 * 1024 && set_smem_optin(reinterpret_cast<const void*>(kern), smem) != KSH_OK)
     return KSH_ERR_CUDA;
   const int64_t nrg = EPI == EPI_SWIGLU ? a.inter : a.n;
   const int64_t grid = (nrg + static_cast<int64_t>(kWarps) * rw - 1) / (static_cast<int64_t>(kWarps) * rw);

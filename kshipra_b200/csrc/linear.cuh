@@ -32,9 +32,38 @@ struct LinArgs {
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
+// Exact integer -> float for packed weights without the int-to-float
+// conversion unit (a quarter-rate pipe that caps a decode GEMV well below HBM
+// speed): an offset-binary byte u (0..255) is moved into the low mantissa
+// bits of 2^23 with one byte permute, giving the float 2^23 + u exactly, and
+// one float add removes 2^23 and the offset.
+//
+// INT8: bias the word once (w ^ 0x80808080: u = q + 128), then dq_i8(wb, b)
+// is q of byte b.
+__device__ __forceinline__ uint32_t bias_i8(uint32_t w) { return w ^ 0x80808080u; }
+__device__ __forceinline__ float dq_i8(uint32_t wb, int b) {
+  return __int_as_float(static_cast<int>(__byte_perm(wb, 0x4B000000u, 0x7540u | b))) -
+         8388736.0f;   // 2^23 + 128
+}
+// INT4 (low nibble = even element): split a word into the low and high
+// nibbles of each byte, biased (u = q + 8); nibble t of the word is byte t/2
+// of lo (t even) or hi (t odd).
+__device__ __forceinline__ uint32_t nib_lo(uint32_t w) { return (w & 0x0F0F0F0Fu) ^ 0x08080808u; }
+__device__ __forceinline__ uint32_t nib_hi(uint32_t w) {
+  return ((w >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+}
+__device__ __forceinline__ float dq_i4(uint32_t nb, int b) {
+  return __int_as_float(static_cast<int>(__byte_perm(nb, 0x4B000000u, 0x7540u | b))) -
+         8388616.0f;   // 2^23 + 8
+}
+
 int launch_gemv(int wk, int epi, const LinArgs& a, cudaStream_t stream);
 // Register-resident decode GEMV for small matrices; false if not applicable.
 bool launch_gemv_resident(int wk, int epi, const LinArgs& a, cudaStream_t stream, int* status);
+// Tensor-core decode path (M <= 16, quantized weights, qgemv_tc.cu).
+bool gemv_tc_eligible(int wk, int epi, const LinArgs& a);
+int launch_gemv_tc(int wk, int epi, const LinArgs& a, cudaStream_t stream);
+int set_gemv_tc_mode(int mode);
 // Force the streaming GEMV (tests compare both paths); returns the previous value.
 int set_gemv_resident_enabled(int on);
 bool gemv_resident_enabled();

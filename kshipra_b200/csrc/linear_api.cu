@@ -35,6 +35,7 @@ bool gemv_ok(int wk, const LinArgs& a) {
 
 int run_linear(int wk, int epi, LinArgs& a, void* ws, int64_t ws_bytes, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a.m <= kGemvMaxM && gemv_tc_eligible(wk, epi, a)) return launch_gemv_tc(wk, epi, a, s);
   if (gemv_ok(wk, a)) return launch_gemv(wk, epi, a, s);
   if (a.m > kGemvMaxM) {
     bool taken = false;

@@ -10,6 +10,7 @@
 
 #include <cudaTypedefs.h>
 
+#include "linear.cuh"
 #include "tc_common.cuh"
 
 namespace ksh {
@@ -143,6 +144,8 @@ extern "C" int ksh_last_cuda_error(void) { return ksh::g_last_cuda_error.load();
 extern "C" int ksh_set_pdl(int enabled) { return ksh::g_pdl.exchange(enabled ? 1 : 0); }
 
 extern "C" int ksh_set_gemv_resident(int enabled) { return ksh::set_gemv_resident_enabled(enabled); }
+
+extern "C" int ksh_set_gemv_tc(int mode) { return ksh::set_gemv_tc_mode(mode); }
 
 extern "C" const char* ksh_status_string(int status) {
   switch (status) {

@@ -144,6 +144,69 @@ def test_linear_paths_residual_and_swiglu(scheme, m):
             _lib.lib().ksh_set_gemv_resident(prev)
 
 
+def _rms_norm64(x, nw, eps=1e-6):
+    x = x.astype(np.float64)
+    return x / np.sqrt((x * x).mean(-1, keepdims=True) + eps) * nw.astype(np.float64)
+
+
+@pytest.mark.parametrize("scheme", ["int8", "int4"])
+@pytest.mark.parametrize("m", [1, 3, 8, 9, 16])
+@pytest.mark.parametrize("K,N,I", [(896, 1152, 640), (912, 1000, 328), (4096, 6144, 1536)])
+def test_tensor_core_decode_linear(scheme, m, K, N, I):
+    """Swap-AB tcgen05 decode path (forced for every shape) against fp64 with
+    the dequantized weight: bias + residual, fused RMSNorm, SwiGLU; tiles that
+    overhang N, K not a multiple of the 64-wide stage."""
+    from kshipra_b200 import _lib
+    from kshipra_b200.quantization import (linear_launch, quantize_int4_per_group,
+                                           quantize_int8_per_channel, swiglu_launch)
+    gen = torch.Generator().manual_seed(m * 31 + K + N)
+    x = torch.randn((m, K), generator=gen)
+    x[0] *= 40.0                               # token rows of very different size
+    w = torch.randn((N, K), generator=gen) * 0.03
+    wgu = torch.randn((2 * I, K), generator=gen) * 0.03
+    res = torch.randn((m, N), generator=gen)
+    bias = torch.randn((N,), generator=gen)
+    nw = 1.0 + 0.2 * torch.randn((K,), generator=gen)
+    if scheme == "int8":
+        qw, qgu = quantize_int8_per_channel(w.cuda()), quantize_int8_per_channel(wgu.cuda())
+        wd = oq.dequantize_int8(*oq.quantize_int8_per_channel(w.numpy()))
+        gud = oq.dequantize_int8(*oq.quantize_int8_per_channel(wgu.numpy()))
+    else:
+        qw, qgu = quantize_int4_per_group(w.cuda()), quantize_int4_per_group(wgu.cuda())
+        p, s, _ = oq.quantize_int4_per_group(w.numpy(), 128)
+        wd = oq.dequantize_int4(p, s, K, 128)
+        p, s, _ = oq.quantize_int4_per_group(wgu.numpy(), 128)
+        gud = oq.dequantize_int4(p, s, K, 128)
+    wd, gud = wd.astype(np.float64), gud.astype(np.float64)
+    x64 = x.double().numpy()
+    xn64 = _rms_norm64(x.numpy(), nw.numpy())
+    y64 = x64 @ wd.T + bias.double().numpy() + res.double().numpy()
+    yn64 = xn64 @ wd.T
+    gu = xn64 @ gud.T
+    h64 = gu[:, :I] / (1 + np.exp(-gu[:, :I])) * gu[:, I:]
+    xc, nc = x.cuda(), nw.cuda()
+    modes = (2, 3) if scheme == "int8" else (2,)    # int8: kind::i8 and fp16 kernels
+    prev = _lib.lib().ksh_set_gemv_tc(2)
+    try:
+        for mode in modes:
+            _lib.lib().ksh_set_gemv_tc(mode)
+            for _ in range(2):
+                y = res.clone().cuda()
+                linear_launch(xc, qw, None, bias.cuda(), y, residual=y)
+                err = np.abs(y.cpu().numpy() - y64).max(axis=1) / np.abs(y64).max(axis=1)
+                assert err.max() <= 2e-5, (mode, err)
+                yn = torch.empty((m, N), device="cuda")
+                linear_launch(xc, qw, None, None, yn, norm_w=nc)
+                err = np.abs(yn.cpu().numpy() - yn64).max(axis=1) / np.abs(yn64).max(axis=1)
+                assert err.max() <= 2e-5, (mode, err)
+                h = torch.empty((m, I), device="cuda")
+                swiglu_launch(xc, qgu, None, I, h, norm_w=nc)
+                err = np.abs(h.cpu().numpy() - h64).max(axis=1) / np.maximum(np.abs(h64).max(axis=1), 1e-3)
+                assert err.max() <= 2e-5, (mode, err)
+    finally:
+        _lib.lib().ksh_set_gemv_tc(prev)
+
+
 def _run_attention_case(q, kp, vp, bt, P, C, B):
     from kshipra_b200.chunked_prefill import chunked_attention
     return chunked_attention(q.cuda(), kp.cuda(), vp.cuda(), bt, P, C, B).cpu()
