@@ -250,14 +250,20 @@ def run_ours(args, wl):
              "d2h_bytes_per_step": d2h},
         roofline={"kernel": "lm_head fp32 GEMV + argmax (ksh_lm_head_argmax)", "bound": "hbm",
                   "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                  "peak_kind": peak_kind, "traffic": None,
+                  "peak_kind": peak_kind,
+                  "traffic": profiled_traffic(f"lm_head_{wl['preset']}"),
+                  "traffic_source": f"profiles/lm_head_{wl['preset']}.md (ncu, one launch)",
                   "algorithmic_bytes_per_launch": lm_bytes, "launch_ms": lm_ms},
         gpu_launches=None,
         clocks=clk.summary(),
     )
+    # this library's kernels per request, as counted in the ncu launch list
+    # (profiles/launches_qwen05b_int8.md): per prefill chunk 10 per layer + the
+    # embedding, one lm_head, per decode step 5 per layer + embedding, lm_head
+    # and the on-device greedy bookkeeping
     n_layers = cfg.layers
-    per_tok = n_layers * 8 + 1 + 2 + 1
-    per_chunk = n_layers * 8 + 2 + 1
+    per_chunk = n_layers * 10 + 1
+    per_tok = n_layers * 5 + 3
     res["gpu_launches"] = args.steps * ((P + C - 1) // C * per_chunk + 1 + (NEW - 1) * per_tok)
     if rank == 0 and not args.no_cpu_baseline and ws == 1:
         res["cpu_baseline"] = cpu_baseline(wl, cfg, prompt, samples=1)
@@ -424,6 +430,54 @@ def run_micro(args):
     print(json.dumps(res))
 
 
+def run_profile_lm_head(args, wl):
+    """The roofline kernel alone, for an ncu capture of a small case: the
+    workload's fp32 lm_head weight [vocab, hidden] (544 MB for the 0.5B shape)
+    and one ksh_lm_head_argmax call (fused final norm + GEMV + argmax, one
+    token row) between cudaProfilerStart/Stop, after a warm-up."""
+    from kshipra_b200 import _lib as L
+    from kshipra_b200.config import PRESETS
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = PRESETS[wl["preset"]]
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = torch.randn((cfg.vocab, cfg.hidden), generator=g, device=dev) * 0.02
+    nw = torch.ones(cfg.hidden, device=dev)
+    x = torch.randn((1, cfg.hidden), generator=g, device=dev)
+    tok = torch.empty(1, dtype=torch.int64, device=dev)
+    ws = torch.zeros(int(L.lib().ksh_lm_head_workspace_size(1, cfg.vocab)), dtype=torch.uint8, device=dev)
+    s = L.stream_ptr()
+
+    def run():
+        L.call("ksh_lm_head_argmax", x.data_ptr(), 1, cfg.hidden, nw.data_ptr(), 1e-6, w.data_ptr(),
+               cfg.vocab, None, tok.data_ptr(), ws.data_ptr(), ws.numel(), s)
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    run()
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"profile": "lm_head", "workload": args.workload,
+                      "algorithmic_bytes": cfg.vocab * cfg.hidden * 4 + cfg.hidden * 8}))
+
+
+def profiled_traffic(name):
+    """DRAM bytes per launch recorded in profiles/<name>.md (line
+    'traffic_bytes_per_launch: N', from ncu dram__bytes_read.sum +
+    dram__bytes_write.sum), or None."""
+    p = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
 def run_profile(args, wl):
     """One request (chunked prefill + decode graph replays) between
     cudaProfilerStart/Stop, after a warm-up, for ncu --profile-from-start off."""
@@ -491,6 +545,8 @@ def main():
                     help="run one request inside cudaProfilerStart/Stop (for ncu)")
     ap.add_argument("--trace", action="store_true",
                     help="with --profile: CUPTI trace of one request, per-kernel summary")
+    ap.add_argument("--profile-kernel", default=None, choices=["lm_head"],
+                    help="with --profile: only this kernel on the workload's shape (small ncu case)")
     ap.add_argument("--micro-filter", default=None,
                     help="micro workload: comma list of scheme:M:KxN points to run")
     args = ap.parse_args()
@@ -498,6 +554,9 @@ def main():
         run_micro(args)
         return
     wl = WORKLOADS[args.workload]
+    if args.profile and args.profile_kernel == "lm_head":
+        run_profile_lm_head(args, wl)
+        return
     if args.profile:
         run_profile(args, wl)
         return

@@ -558,27 +558,38 @@ qgemv_tc_kernel(const __grid_constant__ CUtensorMap map_w, GvArgs a) {
 constexpr int BK8 = 128;                          // K bytes per stage
 constexpr int A8_BYTES = BW * BK8;                // 16 KB
 
-template <int MP>
+template <int MP, int AT>
 struct LayoutI8 {
+  // AT swizzle atoms (128 K bytes each) per stage: 128 * AT contiguous bytes
+  // of every weight row per TMA stage
   static constexpr int NCOL = (3 * MP + 15) / 16 * 16;
-  static constexpr int NS = 4;
-  static constexpr int B_BYTES = NCOL * 128;
+  static constexpr int NS = AT == 1 ? 4 : 2;      // TMA stages
+  static constexpr int KS = BK8 * AT;             // K bytes per stage
+  static constexpr int A_STAGE = A8_BYTES * AT;
+  static constexpr int B_ATOM = NCOL * 128;
+  static constexpr int B_BYTES = B_ATOM * AT;
   static constexpr int A_OFF = 0;
-  static constexpr int B_OFF = A_OFF + NS * A8_BYTES;
+  static constexpr int B_OFF = A_OFF + NS * A_STAGE;
   static constexpr int TILE_OFF = B_OFF + NS * B_BYTES;
   static constexpr int SMALL_OFF = TILE_OFF + BW * MP * 4;
   static constexpr int BAR_OFF = SMALL_OFF + (4 + 8) * MP * 4;
-  static constexpr int BYTES = BAR_OFF + 256;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int BYTES = BAR_OFF + BAR_BYTES;
   static size_t smem(int, int) { return 1024 + static_cast<size_t>(BYTES); }
-  static constexpr uint32_t TMEM_COLS = NCOL <= 32 ? 32 : 64;
+  // Consecutive MMAs rotate over NC accumulator copies: an MMA that adds into
+  // the accumulator the previous one wrote waits for it, and with N this
+  // small that latency, not the math, would set the pace.
+  static constexpr int NC = 4;
+  static constexpr uint32_t TMEM_COLS = NC * NCOL <= 64 ? 64 : (NC * NCOL <= 128 ? 128 : 256);
 };
 
-template <int EPI, int MP>
+template <int EPI, int MP, int AT>
 __global__ void __launch_bounds__(kThreads, 1)
 qgemv_i8_kernel(const __grid_constant__ CUtensorMap map_w, GvArgs a) {
-  using L = LayoutI8<MP>;
+  using L = LayoutI8<MP, AT>;
   constexpr int NCOL = L::NCOL;
   constexpr int NS = L::NS;
+  constexpr int KS = L::KS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* tile = reinterpret_cast<float*>(smem + L::TILE_OFF);
@@ -601,7 +612,7 @@ qgemv_i8_kernel(const __grid_constant__ CUtensorMap map_w, GvArgs a) {
   const int kt_begin = split * a.kt_per_split;
   const int kt_end = min(kt_begin + a.kt_per_split, a.kt_total);
   const int ntl = max(kt_end - kt_begin, 0);
-  auto a_tile = [&](int s) { return smem + L::A_OFF + s * A8_BYTES; };
+  auto a_tile = [&](int s) { return smem + L::A_OFF + s * L::A_STAGE; };
   auto b_tile = [&](int s) { return smem + L::B_OFF + s * L::B_BYTES; };
 
   if (threadIdx.x == 0) {
@@ -630,13 +641,17 @@ qgemv_i8_kernel(const __grid_constant__ CUtensorMap map_w, GvArgs a) {
       const int pre = min(NS, ntl);
       auto issue = [&](int i) {
         const int s = i % NS;
-        mbar_arrive_expect_tx(&full[s], A8_BYTES);
-        const int kg = (kt_begin + i) * BK8;
-        if (EPI == EPI_SWIGLU) {
-          tma_load_2d(a_tile(s), &map_w, &full[s], kg, n_tile * (BW / 2));
-          tma_load_2d(a_tile(s) + A8_BYTES / 2, &map_w, &full[s], kg, a.inter + n_tile * (BW / 2));
-        } else {
-          tma_load_2d(a_tile(s), &map_w, &full[s], kg, n_tile * BW);
+        mbar_arrive_expect_tx(&full[s], L::A_STAGE);
+#pragma unroll
+        for (int at = 0; at < AT; ++at) {
+          const int kg = (kt_begin + i) * KS + at * BK8;
+          uint8_t* dst = a_tile(s) + at * A8_BYTES;
+          if (EPI == EPI_SWIGLU) {
+            tma_load_2d(dst, &map_w, &full[s], kg, n_tile * (BW / 2));
+            tma_load_2d(dst + A8_BYTES / 2, &map_w, &full[s], kg, a.inter + n_tile * (BW / 2));
+          } else {
+            tma_load_2d(dst, &map_w, &full[s], kg, n_tile * BW);
+          }
         }
       };
       for (int i = 0; i < pre; ++i) issue(i);      // constant data: before the wait
@@ -674,9 +689,13 @@ qgemv_i8_kernel(const __grid_constant__ CUtensorMap map_w, GvArgs a) {
         tc_fence_after();
         const uint32_t ad = smem_u32(a_tile(s)), bd = smem_u32(b_tile(s));
 #pragma unroll
-        for (int kk = 0; kk < BK8 / 32; ++kk)
-          mma_i8(tmem, desc_k_sw128(ad + kk * 32), desc_k_sw128(bd + kk * 32), idesc,
-                 (i == 0 && kk == 0) ? 0u : 1u);
+        for (int at = 0; at < AT; ++at)
+#pragma unroll
+          for (int kk = 0; kk < BK8 / 32; ++kk) {
+            const int u = (i * AT + at) * (BK8 / 32) + kk;      // MMA index in this CTA
+            mma_i8(tmem + (u % L::NC) * NCOL, desc_k_sw128(ad + at * A8_BYTES + kk * 32),
+                   desc_k_sw128(bd + at * L::B_ATOM + kk * 32), idesc, u >= L::NC ? 1u : 0u);
+          }
         mma_commit(&empty[s]);
       }
       if (!ok) *abort_flag = 1;
@@ -689,8 +708,8 @@ qgemv_i8_kernel(const __grid_constant__ CUtensorMap map_w, GvArgs a) {
     const int t = threadIdx.x - 64;
     const int q = warp & 3;
     const int row_local = q * 32 + lane;
-    const int k_lo = kt_begin * BK8;
-    const int k_hi = min(kt_end * BK8, a.k);
+    const int k_lo = kt_begin * KS;
+    const int k_hi = min(kt_end * KS, a.k);
     const int wrow = [&]() -> int {
       if (EPI == EPI_SWIGLU) {
         const int c = n_tile * (BW / 2) + (row_local & (BW / 2 - 1));
@@ -701,11 +720,11 @@ qgemv_i8_kernel(const __grid_constant__ CUtensorMap map_w, GvArgs a) {
       return r < a.n ? r : -1;
     }();
     const float wscale = wrow >= 0 ? __half2float(a.scales[wrow]) : 0.0f;
-    x_slice_prologue<MP>(a, nullptr, 0, k_lo, k_hi, ntl * BK8, t, red_mx, red_ss, escale, einv, ss_part, 22);
+    x_slice_prologue<MP>(a, nullptr, 0, k_lo, k_hi, ntl * KS, t, red_mx, red_ss, escale, einv, ss_part, 22);
     // digit rows of tokens >= m, and padding rows >= 3 * MP, stay zero
     for (int i = t; i < NS * L::B_BYTES / 16; i += 128) {
       const int st = i / (L::B_BYTES / 16), rem = i % (L::B_BYTES / 16);
-      const int r = rem / 8;
+      const int r = (rem % (L::B_ATOM / 16)) / 8;      // row within its atom
       if (r >= 3 * MP || (r % MP) >= a.m)
         reinterpret_cast<uint4*>(b_tile(st))[rem] = make_uint4(0u, 0u, 0u, 0u);
     }
@@ -720,9 +739,9 @@ qgemv_i8_kernel(const __grid_constant__ CUtensorMap map_w, GvArgs a) {
       }
       // (token m, 16-element chunk c): three digit rows, 16 bytes each
       // (x comes from L2: the writers run up to NS stages ahead of the MMAs)
-      for (int it = t; it < a.m * 8; it += 128) {
-        const int m = it >> 3, c = it & 7;
-        const int kb = (kt_begin + i) * BK8 + c * 16;   // a.k % 16 == 0: chunks are whole
+      for (int it = t; it < a.m * 8 * AT; it += 128) {
+        const int m = it / (8 * AT), cg = it % (8 * AT), c = cg & 7;
+        const int kb = (kt_begin + i) * KS + cg * 16;   // a.k % 16 == 0: chunks are whole
         float4 xv[4] = {};
         if (kb < a.k) {
           const float4* xr = reinterpret_cast<const float4*>(a.x + static_cast<int64_t>(m) * a.k + kb);
@@ -760,7 +779,7 @@ qgemv_i8_kernel(const __grid_constant__ CUtensorMap map_w, GvArgs a) {
           d1[w] = b1;
           d2[w] = b2;
         }
-        uint8_t* bt = b_tile(s);
+        uint8_t* bt = b_tile(s) + (cg >> 3) * L::B_ATOM;
         const int r0 = m, r1 = MP + m, r2 = 2 * MP + m;
         *reinterpret_cast<uint4*>(bt + (r0 >> 3) * 1024 + (r0 & 7) * 128 + ((c ^ (r0 & 7)) << 4)) =
             make_uint4(d0[0], d0[1], d0[2], d0[3]);
@@ -783,14 +802,19 @@ qgemv_i8_kernel(const __grid_constant__ CUtensorMap map_w, GvArgs a) {
     if (ntl > 0 && mbar_wait(acc_full, 0)) {
       tc_fence_after();
       int dd[NCOL];
+#pragma unroll
+      for (int j = 0; j < NCOL; ++j) dd[j] = 0;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+      const int used = min(L::NC, ntl * AT * (BK8 / 32));     // copies that were written
+      for (int cp = 0; cp < used; ++cp) {
 #pragma unroll
-      for (int c = 0; c < NCOL / 16; ++c) {
-        float v[16];
-        tmem_ld_32x32b_x16(taddr + c * 16, v);
-        tmem_wait_ld();
+        for (int c = 0; c < NCOL / 16; ++c) {
+          float v[16];
+          tmem_ld_32x32b_x16(taddr + cp * NCOL + c * 16, v);
+          tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) dd[c * 16 + j] = __float_as_int(v[j]);
+          for (int j = 0; j < 16; ++j) dd[c * 16 + j] += __float_as_int(v[j]);
+        }
       }
 #pragma unroll
       for (int m = 0; m < MP; ++m)
@@ -941,12 +965,13 @@ int launch_gv(const LinArgs& a, cudaStream_t stream) {
 // kind::i8 kernel (INT8)
 template <int EPI, int MP>
 int launch_gv_i8(const LinArgs& a, cudaStream_t stream) {
-  using L = LayoutI8<MP>;
-  auto kern = qgemv_i8_kernel<EPI, MP>;
+  constexpr int AT = 2;              // 256 contiguous bytes of each weight row per stage
+  using L = LayoutI8<MP, AT>;
+  auto kern = qgemv_i8_kernel<EPI, MP, AT>;
   const void* kp = reinterpret_cast<const void*>(kern);
   if (set_smem_optin(kp, kMaxSmem) != KSH_OK) return KSH_ERR_CUDA;
   const int m = static_cast<int>(a.m);
-  const GvPlan p = gv_plan(EPI, a.k, a.n, BK8, 1,
+  const GvPlan p = gv_plan(EPI, a.k, a.n, L::KS, 1,
                            [&](int kps) { return gv_slots(kp, L::smem(m, kps)); });
   if (p.splits < 1) return KSH_ERR_UNSUPPORTED;
   CUtensorMap mw;
@@ -1008,7 +1033,7 @@ bool gemv_tc_eligible(int wk, int epi, const LinArgs& a) {
   const int64_t keff = wk == WK_I4 ? a.kp : a.k;
   // the x slice of the largest split must fit shared memory (bound over both kernels)
   const int64_t k_split = (keff + kMaxSplits - 1) / kMaxSplits + 2 * BK8;
-  const size_t worst = 1024 + static_cast<size_t>(std::max(Layout<WK_I4, 16>::BYTES, LayoutI8<16>::BYTES)) +
+  const size_t worst = 1024 + static_cast<size_t>(std::max(Layout<WK_I4, 16>::BYTES, LayoutI8<16, 2>::BYTES)) +
                        static_cast<size_t>(a.m) * k_split * 4;
   if (worst > kMaxSmem) return false;
   if (mode >= 2) return true;
