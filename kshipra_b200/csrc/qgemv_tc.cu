@@ -839,12 +839,356 @@ qgemv_i8_kernel(const __grid_constant__ CUtensorMap map_w, GvArgs a) {
   grid_dep_launch();
 }
 
+
+// ---------------------------------------------------------------------------
+// INT4: kind::i8 MMAs on nibbles sign-extended to bytes, per-group promotion
+// ---------------------------------------------------------------------------
+//
+// One 128-wide K step is one quantization group (G = 128).  Converter warps
+// widen each raw 64-byte row (128 nibbles) to 128 signed bytes; within every
+// 16-element chunk the byte order is [0,2,4,6,1,3,5,7,8,10,12,14,9,11,13,15]
+// (low nibbles, then high nibbles, of each 32-bit word), and the token digits
+// use the same order.  Each group's MMAs accumulate into their own TMEM
+// buffer (two, alternating); the converter warps read it back (int32, |D| <=
+// 2^17, converted exactly through the 1.5 * 2^23 constant) and add it, times
+// the group scale, to register accumulators.  A seventh warp writes the
+// token digits, running ahead of the MMAs.
+constexpr int kThreadsI4 = 224;
+constexpr int RAW4_BYTES = BW * BK8 / 2;          // 8 KB: 128 rows x 64 bytes
+
+template <int MP>
+struct LayoutI4 {
+  static constexpr int NCOL = (3 * MP + 15) / 16 * 16;
+  static constexpr int RS = 4;                    // raw TMA stages
+  static constexpr int NA4 = 3;                   // widened operand slots
+  static constexpr int NB4 = 3;                   // token digit slots
+  static constexpr int B_BYTES = NCOL * 128;
+  static constexpr int RAW_OFF = 0;
+  static constexpr int A_OFF = RAW_OFF + RS * RAW4_BYTES;
+  static constexpr int B_OFF = A_OFF + NA4 * A8_BYTES;
+  static constexpr int TILE_OFF = B_OFF + NB4 * B_BYTES;
+  static constexpr int SMALL_OFF = TILE_OFF + BW * MP * 4;
+  static constexpr int BAR_OFF = SMALL_OFF + (4 + 8) * MP * 4;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int BYTES = BAR_OFF + BAR_BYTES;
+  static size_t smem(int, int) { return 1024 + static_cast<size_t>(BYTES); }
+  static constexpr uint32_t TMEM_COLS = 2 * NCOL <= 32 ? 32 : (2 * NCOL <= 64 ? 64 : 128);
+};
+
+__device__ __forceinline__ uint32_t s4_lo_bytes(uint32_t w) {
+  return ((((w & 0x0F0F0F0Fu) ^ 0x08080808u) + 0x78787878u) ^ 0x80808080u);
+}
+__device__ __forceinline__ uint32_t s4_hi_bytes(uint32_t w) {
+  return (((((w >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u) + 0x78787878u) ^ 0x80808080u);
+}
+// exact int -> float for |v| < 2^22
+__device__ __forceinline__ float i2f_small(int v) {
+  return __int_as_float(v + 0x4B400000) - 12582912.0f;
+}
+
+template <int EPI, int MP>
+__global__ void __launch_bounds__(kThreadsI4, 1)
+qgemv_i4_kernel(const __grid_constant__ CUtensorMap map_w, GvArgs a) {
+  using L = LayoutI4<MP>;
+  constexpr int NCOL = L::NCOL;
+  constexpr int RS = L::RS, NA4 = L::NA4, NB4 = L::NB4;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* tile = reinterpret_cast<float*>(smem + L::TILE_OFF);
+  float* escale = reinterpret_cast<float*>(smem + L::SMALL_OFF);
+  float* einv = escale + MP;
+  float* ss_part = einv + MP;
+  float* inv_s = ss_part + MP;
+  float* red_mx = inv_s + MP;
+  float* red_ss = red_mx + 4 * MP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* full = bars;               // [RS]  raw tile landed
+  uint64_t* rempty = full + RS;        // [RS]  converters done with the raw tile
+  uint64_t* aready = rempty + RS;      // [NA4] widened weights written
+  uint64_t* afree = aready + NA4;      // [NA4] MMAs done with them
+  uint64_t* bready = afree + NA4;      // [NB4] token digits written
+  uint64_t* bfree = bready + NB4;      // [NB4] MMAs done with them
+  uint64_t* acc_full = bfree + NB4;    // [2]
+  uint64_t* acc_empty = acc_full + 2;  // [2]
+  uint64_t* xready = acc_empty + 2;    // [1]   per-token scales known
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xready + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  static_assert((2 * RS + 2 * NA4 + 2 * NB4 + 4 + 1) * 8 + 8 <= L::BAR_BYTES, "barrier region");
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, split = blockIdx.y;
+  const int kt_begin = split * a.kt_per_split;
+  const int kt_end = min(kt_begin + a.kt_per_split, a.kt_total);
+  const int ntl = max(kt_end - kt_begin, 0);
+  auto raw_tile = [&](int s) { return smem + L::RAW_OFF + s * RAW4_BYTES; };
+  auto a_tile = [&](int s) { return smem + L::A_OFF + s * A8_BYTES; };
+  auto b_tile = [&](int s) { return smem + L::B_OFF + s * L::B_BYTES; };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&rempty[s], 128);
+    }
+    for (int s = 0; s < NA4; ++s) {
+      mbar_init(&aready[s], 128);
+      mbar_init(&afree[s], 1);
+    }
+    for (int s = 0; s < NB4; ++s) {
+      mbar_init(&bready[s], 32);
+      mbar_init(&bfree[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(xready, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&map_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer: raw int4 tiles ----------------
+    if (lane == 0) {
+      const int pre = min(RS, ntl);
+      auto issue = [&](int i) {
+        const int s = i % RS;
+        mbar_arrive_expect_tx(&full[s], RAW4_BYTES);
+        const int xb = (kt_begin + i) * (BK8 / 2);
+        if (EPI == EPI_SWIGLU) {
+          tma_load_2d(raw_tile(s), &map_w, &full[s], xb, n_tile * (BW / 2));
+          tma_load_2d(raw_tile(s) + RAW4_BYTES / 2, &map_w, &full[s], xb, a.inter + n_tile * (BW / 2));
+        } else {
+          tma_load_2d(raw_tile(s), &map_w, &full[s], xb, n_tile * BW);
+        }
+      };
+      for (int i = 0; i < pre; ++i) issue(i);      // constant data: before the wait
+      grid_dep_wait();
+      grid_dep_launch();
+      int issued = pre;
+      for (int i = pre; i < ntl && !*abort_flag; ++i) {
+        const int s = i % RS;
+        if (!mbar_wait(&rempty[s], ((i / RS) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        issue(i);
+        issued = i + 1;
+      }
+      if (*abort_flag)
+        for (int i = max(0, issued - RS); i < issued; ++i) mbar_wait(&full[i % RS], (i / RS) & 1);
+    } else {
+      grid_dep_wait();
+      grid_dep_launch();
+    }
+  } else if (warp == 1) {
+    // ---------------- single-thread MMA issue ----------------
+    grid_dep_wait();
+    grid_dep_launch();
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_s8_s32(BW, NCOL);
+      bool ok = true;
+      for (int i = 0; i < ntl && !*abort_flag; ++i) {
+        const int sa = i % NA4, sb = i % NB4, buf = i & 1;
+        if ((i >= 2 && !mbar_wait(&acc_empty[buf], ((i >> 1) - 1) & 1)) ||
+            !mbar_wait(&aready[sa], (i / NA4) & 1) || !mbar_wait(&bready[sb], (i / NB4) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t ad = smem_u32(a_tile(sa)), bd = smem_u32(b_tile(sb));
+        const uint32_t d = tmem + buf * NCOL;
+#pragma unroll
+        for (int kk = 0; kk < BK8 / 32; ++kk)
+          mma_i8(d, desc_k_sw128(ad + kk * 32), desc_k_sw128(bd + kk * 32), idesc, kk ? 1u : 0u);
+        mma_commit(&afree[sa]);
+        mma_commit(&bfree[sb]);
+        mma_commit(&acc_full[buf]);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp == 6) {
+    // ---------------- token digits (32 threads) ----------------
+    grid_dep_wait();
+    grid_dep_launch();
+    bool ok = mbar_wait(xready, 0);
+    for (int i = 0; i < ntl && ok; ++i) {
+      const int sb = i % NB4;
+      if (*abort_flag || (i >= NB4 && !mbar_wait(&bfree[sb], ((i / NB4) - 1) & 1))) {
+        ok = false;
+        break;
+      }
+      for (int it = lane; it < a.m * 8; it += 32) {
+        const int m = it >> 3, c = it & 7;
+        const int kb = (kt_begin + i) * BK8 + c * 16;
+        float xv[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) xv[j] = 0.0f;
+        if (kb + 16 <= a.k) {
+          const float4* xr = reinterpret_cast<const float4*>(a.x + static_cast<int64_t>(m) * a.k + kb);
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const float4 v = xr[w];
+            xv[4 * w] = v.x; xv[4 * w + 1] = v.y; xv[4 * w + 2] = v.z; xv[4 * w + 3] = v.w;
+          }
+        } else {
+          for (int j = 0; j < 16; ++j)
+            if (kb + j < a.k) xv[j] = a.x[static_cast<int64_t>(m) * a.k + kb + j];
+        }
+        if (a.norm_w) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (kb + j < a.k) xv[j] *= a.norm_w[kb + j];
+        }
+        const float es = escale[m];
+        uint32_t d0[4] = {}, d1[4] = {}, d2[4] = {};
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+          // byte p holds element [0,2,4,6,1,3,5,7,...] of the chunk
+          const int e = (p & 8) + ((p & 3) << 1) + ((p >> 2) & 1);
+          const int X = __float_as_int(fmaf(xv[e], es, 12582912.0f)) - 0x4B400000;
+          const int c0 = ((X + 128) & 255) - 128;
+          const int X1 = (X - c0) >> 8;
+          const int c1 = ((X1 + 128) & 255) - 128;
+          const int c2 = (X1 - c1) >> 8;
+          d0[p >> 2] |= (static_cast<uint32_t>(c0) & 0xFFu) << (8 * (p & 3));
+          d1[p >> 2] |= (static_cast<uint32_t>(c1) & 0xFFu) << (8 * (p & 3));
+          d2[p >> 2] |= (static_cast<uint32_t>(c2) & 0xFFu) << (8 * (p & 3));
+        }
+        uint8_t* bt = b_tile(sb);
+        const int r0 = m, r1 = MP + m, r2 = 2 * MP + m;
+        *reinterpret_cast<uint4*>(bt + (r0 >> 3) * 1024 + (r0 & 7) * 128 + ((c ^ (r0 & 7)) << 4)) =
+            make_uint4(d0[0], d0[1], d0[2], d0[3]);
+        *reinterpret_cast<uint4*>(bt + (r1 >> 3) * 1024 + (r1 & 7) * 128 + ((c ^ (r1 & 7)) << 4)) =
+            make_uint4(d1[0], d1[1], d1[2], d1[3]);
+        *reinterpret_cast<uint4*>(bt + (r2 >> 3) * 1024 + (r2 & 7) * 128 + ((c ^ (r2 & 7)) << 4)) =
+            make_uint4(d2[0], d2[1], d2[2], d2[3]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bready[sb]);
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      raise_flag(a.flags, KSH_FLAG_TIMEOUT);
+    }
+  } else {
+    // ---------------- converters + promotion + epilogue (128 threads) ----------------
+    grid_dep_wait();
+    grid_dep_launch();
+    const int t = threadIdx.x - 64;
+    const int q = warp & 3;
+    const int row_local = q * 32 + lane;
+    const int k_lo = kt_begin * BK8;
+    const int k_hi = min(kt_end * BK8, a.k);
+    const int wrow = [&]() -> int {
+      if (EPI == EPI_SWIGLU) {
+        const int c = n_tile * (BW / 2) + (row_local & (BW / 2 - 1));
+        if (c >= a.inter) return -1;
+        return row_local < BW / 2 ? c : a.inter + c;
+      }
+      const int r = n_tile * BW + row_local;
+      return r < a.n ? r : -1;
+    }();
+    x_slice_prologue<MP>(a, nullptr, 0, k_lo, k_hi, ntl * BK8, t, red_mx, red_ss, escale, einv, ss_part, 22);
+    for (int i = t; i < NB4 * L::B_BYTES / 16; i += 128) {
+      const int st = i / (L::B_BYTES / 16), rem = i % (L::B_BYTES / 16);
+      const int r = rem / 8;
+      if (r >= 3 * MP || (r % MP) >= a.m)
+        reinterpret_cast<uint4*>(b_tile(st))[rem] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    fence_proxy_async_smem();
+    conv_bar();
+    if (t == 0) mbar_arrive(xready);
+
+    auto group_scale = [&](int i) -> float {
+      return wrow >= 0 ? __half2float(a.scales[static_cast<int64_t>(wrow) * a.ngroups_row + kt_begin + i])
+                       : 0.0f;
+    };
+    float acc[NCOL];
+#pragma unroll
+    for (int j = 0; j < NCOL; ++j) acc[j] = 0.0f;
+    float sc_next = ntl > 0 ? group_scale(0) : 0.0f;
+    auto promote = [&](int i) -> bool {
+      const int buf = i & 1;
+      const float sc = sc_next;
+      if (i + 1 < ntl) sc_next = group_scale(i + 1);
+      if (!mbar_wait(&acc_full[buf], (i >> 1) & 1)) return false;
+      tc_fence_after();
+      const uint32_t taddr = tmem + buf * NCOL + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll
+      for (int c = 0; c < NCOL / 16; ++c) {
+        float v[16];
+        tmem_ld_32x32b_x16(taddr + c * 16, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[c * 16 + j] = fmaf(i2f_small(__float_as_int(v[j])), sc, acc[c * 16 + j]);
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+      return true;
+    };
+
+    bool ok = true;
+    for (int i = 0; i < ntl && ok; ++i) {
+      const int s = i % RS, sa = i % NA4;
+      if (*abort_flag || !mbar_wait(&full[s], (i / RS) & 1) ||
+          (i >= NA4 && !mbar_wait(&afree[sa], ((i / NA4) - 1) & 1))) {
+        ok = false;
+        break;
+      }
+      // raw row t (64 bytes, TMA 64B swizzle: chunk j at j ^ ((t >> 1) & 3)) ->
+      // 128 signed bytes (128B swizzle: chunk c at c ^ (t & 7))
+      const uint8_t* src = raw_tile(s) + t * 64;
+      uint8_t* dst = a_tile(sa) + (t >> 3) * 1024 + (t & 7) * 128;
+      const uint32_t rs = static_cast<uint32_t>((t >> 1) & 3), rsw = static_cast<uint32_t>(t & 7);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 w = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(j) ^ rs) << 4));
+        const uint4 o0 = make_uint4(s4_lo_bytes(w.x), s4_hi_bytes(w.x), s4_lo_bytes(w.y), s4_hi_bytes(w.y));
+        const uint4 o1 = make_uint4(s4_lo_bytes(w.z), s4_hi_bytes(w.z), s4_lo_bytes(w.w), s4_hi_bytes(w.w));
+        *reinterpret_cast<uint4*>(dst + (((2 * j) ^ rsw) << 4)) = o0;
+        *reinterpret_cast<uint4*>(dst + (((2 * j + 1) ^ rsw) << 4)) = o1;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&aready[sa]);
+      mbar_arrive(&rempty[s]);
+      if (i >= 1 && !promote(i - 1)) ok = false;
+    }
+    if (ok && ntl > 0 && !*abort_flag) ok = promote(ntl - 1);
+    if (!ok) {
+      *abort_flag = 1;
+      raise_flag(a.flags, KSH_FLAG_TIMEOUT);
+    }
+#pragma unroll
+    for (int m = 0; m < MP; ++m)
+      tile[row_local * MP + m] =
+          wrow >= 0 ? fmaf(65536.0f, acc[2 * MP + m], fmaf(256.0f, acc[MP + m], acc[m])) * einv[m] : 0.0f;
+  }
+
+  splitk_epilogue<EPI, MP, kThreadsI4>(a, tile, ss_part, inv_s, n_tile, split);
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, L::TMEM_COLS);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 
 // 0: off; 1: auto (by scheme, token count and matrix size); 2: every eligible
-// shape; 3: as 2, with INT8 through the fp16 kernel (for tests)
+// shape; 3: as 2, through the fp16-operand kernel (for tests)
 std::atomic<int> g_gemv_tc{-1};
 
 struct GvPlan {
@@ -888,10 +1232,10 @@ constexpr size_t kMaxSmem = 227 * 1024;
 
 // CTAs of `kern` resident per SM at `smem` bytes: the smaller of the
 // occupancy query and the shared-memory bound (both CTAs' reservations).
-int64_t gv_slots(const void* kern, size_t smem) {
+int64_t gv_slots(const void* kern, size_t smem, int threads = kThreads) {
   if (smem > kMaxSmem) return 0;
   const int by_smem = static_cast<int>((228 * 1024) / (smem + 1024));
-  const int occ = resident_ctas(kern, kThreads, smem);
+  const int occ = resident_ctas(kern, threads, smem);
   return static_cast<int64_t>(num_sms()) * std::max(1, std::min(by_smem, std::max(occ, 1)));
 }
 
@@ -919,10 +1263,10 @@ GvArgs gv_args(const LinArgs& a, const GvPlan& p, int ngroups_row) {
 // One launch: grid (tiles, splits), the splits of a tile as one cluster.
 template <typename Kern>
 int gv_launch(Kern kern, const GvPlan& p, size_t smem, cudaStream_t stream, const CUtensorMap& mw,
-              const GvArgs& g) {
+              const GvArgs& g, int threads = kThreads) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.tiles), static_cast<unsigned>(p.splits), 1);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -980,6 +1324,32 @@ int launch_gv_i8(const LinArgs& a, cudaStream_t stream) {
                           CU_TENSOR_MAP_SWIZZLE_128B))
     return KSH_ERR_CUDA;
   return gv_launch(kern, p, L::smem(m, p.kt_per_split), stream, mw, gv_args(a, p, 1));
+}
+
+// kind::i8 kernel for INT4 (group size 128)
+template <int EPI, int MP>
+int launch_gv_i4(const LinArgs& a, cudaStream_t stream) {
+  using L = LayoutI4<MP>;
+  auto kern = qgemv_i4_kernel<EPI, MP>;
+  const void* kp = reinterpret_cast<const void*>(kern);
+  if (set_smem_optin(kp, kMaxSmem) != KSH_OK) return KSH_ERR_CUDA;
+  const GvPlan p = gv_plan(EPI, a.kp, a.n, BK8, 1,
+                           [&](int kps) { return gv_slots(kp, L::smem(0, kps), kThreadsI4); });
+  if (p.splits < 1) return KSH_ERR_UNSUPPORTED;
+  CUtensorMap mw;
+  const uint32_t box_rows = EPI == EPI_SWIGLU ? BW / 2 : BW;
+  if (!make_tensor_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.kp / 2, a.n, a.kp / 2, BK8 / 2,
+                          box_rows, CU_TENSOR_MAP_SWIZZLE_64B))
+    return KSH_ERR_CUDA;
+  return gv_launch(kern, p, L::smem(0, 0), stream, mw, gv_args(a, p, static_cast<int>(a.kp / a.g)),
+                   kThreadsI4);
+}
+
+template <int EPI>
+int launch_gv_i4_m(const LinArgs& a, cudaStream_t stream) {
+  if (a.m <= 5) return launch_gv_i4<EPI, 5>(a, stream);
+  if (a.m <= 10) return launch_gv_i4<EPI, 10>(a, stream);
+  return launch_gv_i4<EPI, 16>(a, stream);
 }
 
 template <int WK, int EPI>
@@ -1047,7 +1417,10 @@ bool gemv_tc_eligible(int wk, int epi, const LinArgs& a) {
     if (a.m <= 7) return wbytes >= 2 * MiB;
     return wbytes >= MiB / 2;
   }
-  return a.m >= 8 && wbytes >= MiB;
+  // INT4 (integer-MMA kernel for G = 128)
+  if (a.m <= 2) return wbytes >= 24 * MiB;
+  if (a.m <= 7) return wbytes >= 2 * MiB;
+  return wbytes >= MiB;
 }
 
 int launch_gemv_tc(int wk, int epi, const LinArgs& a, cudaStream_t stream) {
@@ -1058,6 +1431,9 @@ int launch_gemv_tc(int wk, int epi, const LinArgs& a, cudaStream_t stream) {
     return epi == EPI_SWIGLU ? launch_gv_i8_m<EPI_SWIGLU>(a, stream)
                              : launch_gv_i8_m<EPI_STORE>(a, stream);
   }
+  if (gemv_tc_mode() != 3 && a.g == BK8)
+    return epi == EPI_SWIGLU ? launch_gv_i4_m<EPI_SWIGLU>(a, stream)
+                             : launch_gv_i4_m<EPI_STORE>(a, stream);
   return epi == EPI_SWIGLU ? launch_gv_m<WK_I4, EPI_SWIGLU>(a, stream)
                            : launch_gv_m<WK_I4, EPI_STORE>(a, stream);
 }

@@ -352,6 +352,67 @@ class KshipraModel:
         return tok
 
     @torch.inference_mode()
+    def run_batch(self, pool: torch.Tensor, seqs) -> List[Optional[int]]:
+        """One forward pass over several sequences at once (continuous batching).
+
+        ``seqs`` holds ``(tokens, start_pos, block_table, want_token)`` per
+        sequence: a decode step (one token at its position) or a prefill chunk
+        (the prompt tokens ``[start_pos, start_pos + len)``).  All of them go
+        through one varlen pass of the kernels; each writes its K/V into its own
+        blocks of ``pool`` and attends over its positions ``[0, start_pos +
+        len)``.  Returns, per sequence, the greedy next token after its last
+        input token when ``want_token`` is set, else None.  This is the batched
+        step the reference's ContinuousEngine only simulates
+        (engine/continuous.py:229-261); the token of a sequence is the one
+        ``generate`` produces for it."""
+        if not seqs:
+            return []
+        dev = self.device
+        bs = pool.shape[4]
+        n = len(seqs)
+        lens = [len(t) for t, _, _, _ in seqs]
+        if min(lens) < 1:
+            raise ValueError("every sequence of a batch needs at least one token")
+        ids, pos, slots = [], [], []
+        for (toks, start, bt, _), c in zip(seqs, lens):
+            ids.extend(int(x) for x in toks)
+            for p in range(start, start + c):
+                if p // bs >= len(bt):
+                    raise IndexError(f"position {p} lies past the sequence's block table")
+                pos.append(p)
+                slots.append(bt[p // bs] * bs + p % bs)
+        max_blocks = max(len(bt) for _, _, bt, _ in seqs)
+        bt_rows = [list(bt) + [0] * (max_blocks - len(bt)) for _, _, bt, _ in seqs]
+        q_start = [0]
+        for c in lens:
+            q_start.append(q_start[-1] + c)
+        T = q_start[-1]
+        ids_t = torch.as_tensor(ids, dtype=torch.int64).to(dev)
+        pos_t = torch.as_tensor(pos, dtype=torch.int64).to(dev)
+        slots_t = torch.as_tensor(slots, dtype=torch.int64).to(dev)
+        bt_t = torch.as_tensor(bt_rows, dtype=torch.int32).to(dev)
+        qs_t = torch.as_tensor(q_start, dtype=torch.int32).to(dev)
+        pl_t = torch.as_tensor([s for _, s, _, _ in seqs], dtype=torch.int32).to(dev)
+        max_total = max(s + c for (_, s, _, _), c in zip(seqs, lens))
+        acts = self._alloc_acts(T)
+        hid = self._run_layers(acts, ids_t, pos_t, slots_t, bt_t, qs_t, pl_t, n, max(lens),
+                               max_total, pool, self._lin_ws, self._attn_ws)
+        want = [i for i, (_, _, _, w) in enumerate(seqs) if w]
+        out: List[Optional[int]] = [None] * n
+        if want:
+            rows = torch.as_tensor([q_start[i + 1] - 1 for i in want], dtype=torch.int64,
+                                   device=dev)
+            x = hid.index_select(0, rows)
+            tok = torch.empty(len(want), dtype=torch.int64, device=dev)
+            for c0 in range(0, len(want), 16):       # the fused argmax takes up to 16 rows
+                c1 = min(c0 + 16, len(want))
+                self._lm_head_argmax(x[c0:c1], tok[c0:c1])
+            for i, t in zip(want, tok.tolist()):
+                out[i] = t
+        _check_flags(self.flags)
+        return out
+
+    @torch.inference_mode()
     def generate(self, prompt_ids: List[int], max_new_tokens: int = 20,
                  eos_token_id: Optional[int] = None, block_size: int = 64,
                  prefill_chunk: Optional[int] = None, use_graph: bool = True) -> List[int]:

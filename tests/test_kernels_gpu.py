@@ -185,7 +185,7 @@ def test_tensor_core_decode_linear(scheme, m, K, N, I):
     gu = xn64 @ gud.T
     h64 = gu[:, :I] / (1 + np.exp(-gu[:, :I])) * gu[:, I:]
     xc, nc = x.cuda(), nw.cuda()
-    modes = (2, 3) if scheme == "int8" else (2,)    # int8: kind::i8 and fp16 kernels
+    modes = (2, 3)       # integer-MMA kernels, then the fp16-operand kernel
     prev = _lib.lib().ksh_set_gemv_tc(2)
     try:
         for mode in modes:

@@ -135,3 +135,58 @@ def test_qwen05b_tokens_match_reference(golden, qwen_sd, scheme):
         pos += 128
     err = logit_err(logits[0, -1].cpu(), g[f"{scheme}/logits0"])
     assert err < LOGIT_RTOL, err
+
+
+def _engine_run(km, prompts, new_tokens, block_size=16, budget_tokens=48, num_blocks=256):
+    """Drive the continuous-batching scheduler with the real batched forward."""
+    from kshipra_b200.continuous import ContinuousEngine
+    from kshipra_b200.prefix_cache import PrefixCache
+    cfg = km.cfg
+    cache = PrefixCache(num_blocks, block_size, cfg.layers, cfg.kv_heads, cfg.head_dim,
+                        dtype=torch.float32, device=torch.device("cuda"))
+    eng = ContinuousEngine(cache, block_size=block_size, max_batch_tokens=budget_tokens,
+                           itl_budget_s=budget_tokens * 1e-3, t_tok_s=1e-3, model=km)
+    reqs = [eng.add_request(list(p), new_tokens) for p in prompts]
+    for _ in range(10000):
+        if all(r in eng.finished for r in reqs):
+            break
+        eng.step()
+    return reqs
+
+
+@pytest.mark.parametrize("scheme", ["int8", "int4"])
+def test_continuous_engine_batched_forward_matches_generate(tiny_sd, scheme):
+    """Requests of different lengths prefill in chunks and decode together in
+    the same batched passes; each one's greedy tokens equal those of running
+    it alone through generate()."""
+    km = KshipraModel(config=TINY_LLAMA, state_dict=tiny_sd, quantize=scheme)
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, TINY_LLAMA.vocab, (n,), generator=g).tolist()
+               for n in (20, 33, 7, 50, 16)]
+    reqs = _engine_run(km, prompts, new_tokens=6)
+    for p, r in zip(prompts, reqs):
+        assert len(r.generated_tokens) == 6
+        solo = km.generate(p, max_new_tokens=6, block_size=16)
+        assert r.generated_tokens == solo, (len(p), r.generated_tokens, solo)
+
+
+def test_run_batch_mixed_prefill_and_decode_vs_oracle(tiny_sd):
+    """One pass holding a prefill chunk and decode steps of other sequences
+    gives each sequence the oracle's next token."""
+    km = KshipraModel(config=TINY_LLAMA, state_dict=tiny_sd, quantize="int8")
+    om = OracleModel(TINY_LLAMA, tiny_sd, quantize="int8")
+    alloc = km.new_pool(64, 16)
+    pool = alloc.pool
+    g = torch.Generator().manual_seed(11)
+    pa = torch.randint(0, TINY_LLAMA.vocab, (21,), generator=g).tolist()
+    pb = torch.randint(0, TINY_LLAMA.vocab, (9,), generator=g).tolist()
+    bta = [alloc.alloc() for _ in range(3)]
+    btb = [alloc.alloc() for _ in range(3)]
+    # a: whole prompt first; b: first 5 prompt tokens, then the rest with a's decode
+    ta = km.run_batch(pool, [(pa, 0, bta, True), (pb[:5], 0, btb, False)])
+    assert ta[1] is None
+    out = km.run_batch(pool, [([ta[0]], len(pa), bta, True), (pb[5:], 5, btb, True)])
+    ref_a = om.generate(pa, 2)
+    ref_b = om.generate(pb, 1)
+    assert [ta[0], out[0]] == ref_a
+    assert out[1] == ref_b[0]
