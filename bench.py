@@ -39,6 +39,12 @@ WORKLOADS = {
     "qwen05b-int4": dict(preset="qwen2.5-0.5b", quantize="int4", prompt=512, chunk=128, new=50,
                          block=16),
     "tiny-int8": dict(preset="tiny-llama", quantize="int8", prompt=32, chunk=16, new=16, block=16),
+    # config 4: Llama-3-8B shape, decode batch 64 at context 4096 (+ one
+    # 2048-token prefill chunk), tensor parallel over the ranks
+    "llama8b-int4": dict(preset="llama-3-8b", quantize="int4", batch=64, context=4096,
+                         prefill=2048, block=16, tp=True),
+    "llama8b-int8": dict(preset="llama-3-8b", quantize="int8", batch=64, context=4096,
+                         prefill=2048, block=16, tp=True),
 }
 
 
@@ -320,6 +326,10 @@ def run_reference(args, wl):
     ws, rank, local = dist_env()
     if rank != 0:
         return None, rank
+    if wl.get("tp"):
+        return {"impl": "reference", "unavailable": "the CPU port is timed on the qwen05b "
+                "workloads; an 8B batch-64 decode at context 4096 does not finish on the host "
+                "cores in minutes"}, rank
     from kshipra_b200.config import PRESETS
     cfg = PRESETS[wl["preset"]]
     g = torch.Generator().manual_seed(0)
@@ -428,6 +438,168 @@ def run_micro(args):
                peaks={"hbm_gbs": hbm, "tensor_tflops": tc_peak, "kind": peak_kind},
                sweep=results)
     print(json.dumps(res))
+
+
+def run_tp(args, wl):
+    """Config 4: batched greedy decode of the 8B shape, tensor parallel.
+
+    Every rank holds 1/N of the heads, intermediate rows and vocabulary; one
+    step is one decode token for all ``batch`` sequences (a CUDA-graph replay
+    of embedding -> 32 layers with two NCCL all-reduces each -> vocabulary-
+    parallel lm_head + argmax -> on-device position advance).  The K/V cache
+    of the ``context`` earlier positions is filled with synthetic values (the
+    decode cost does not depend on them); the 2048-token prefill chunk is
+    timed separately.  value = batch tokens per step / step time (whole job),
+    strong scaling: the same batch over more GPUs."""
+    from kshipra_b200 import _lib as L
+    from kshipra_b200.config import PRESETS
+    from kshipra_b200.model import DecodeState, KshipraModel
+    from kshipra_b200.weights import synthetic_state_dict
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+    cfg = PRESETS[wl["preset"]]
+    sd = synthetic_state_dict(cfg, seed=0, device=dev)          # the same weights on every rank
+    km = KshipraModel(config=cfg, state_dict=sd, quantize=wl["quantize"], device=dev,
+                      tp=(rank, ws, None) if ws > 1 else None)
+    del sd
+    torch.cuda.empty_cache()
+    Bt, ctx, bs, PF = wl["batch"], wl["context"], wl["block"], wl["prefill"]
+    steps_total = max(args.warmup, 3) + args.steps + 4
+    nbs = (ctx + steps_total + bs) // bs + 1
+    npf = (PF + bs - 1) // bs + 1
+    alloc = km.new_pool(Bt * nbs + npf, bs)
+    pool = alloc.pool
+    pool.uniform_(-1.0, 1.0)                                    # synthetic K/V of the context
+    bts = [list(range(i * nbs, (i + 1) * nbs)) for i in range(Bt)]
+    st = DecodeState(km, pool, bts, steps_total)
+    g = torch.Generator().manual_seed(1)
+    first = torch.randint(0, cfg.vocab, (Bt,), generator=g).to(dev)
+    st.start(first, [ctx] * Bt)
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    st.step_eager()
+    graph = True
+    try:
+        st.capture()
+    except Exception as e:                                      # eager steps if capture fails
+        graph = False
+        if rank == 0:
+            print(f"# decode graph capture failed, eager steps: {e}", file=sys.stderr)
+    step = (lambda: st.graph.replay()) if graph else st.step_eager
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+
+    # end to end: every step the batch's input tokens come from pinned host
+    # memory and the generated tokens are read back
+    h_in = torch.randint(0, cfg.vocab, (Bt,), generator=g).pin_memory()
+    h_out = torch.empty(Bt, dtype=torch.int64).pin_memory()
+    barrier()
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(stream)
+    for _ in range(min(args.steps, 4)):
+        st.ids.copy_(h_in, non_blocking=True)
+        step()
+        h_out.copy_(st.next, non_blocking=True)
+    a1.record(stream)
+    barrier()
+    e2e_ms = a0.elapsed_time(a1) / min(args.steps, 4)
+
+    # dominant kernel: decode attention of one layer, timed alone
+    nb_, L_, _, hkv, bs_, d = pool.shape
+    rc, rs = km._rope_tables()
+    qkv = st.acts["qkv"]
+    attn = st.acts["attn"]
+
+    def attn_once():
+        L.call("ksh_decode_attention", qkv.data_ptr(), Bt, km.n_heads, km.n_kv_heads, d,
+               st.positions.data_ptr(), st.slots.data_ptr(), rc.data_ptr(), rs.data_ptr(),
+               rc.shape[0], pool.data_ptr(), nb_, L_, 0, bs_, st.block_tables.data_ptr(),
+               st.block_tables.shape[1], st.capacity, attn.data_ptr(), km.flags.data_ptr(),
+               L.stream_ptr())
+    for _ in range(3):
+        attn_once()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    R = 20
+    r0.record(stream)
+    for _ in range(R):
+        attn_once()
+    r1.record(stream)
+    torch.cuda.synchronize()
+    attn_ms = r0.elapsed_time(r1) / R
+    ctx_now = int(st.positions[0]) + 1
+    attn_bytes = Bt * ctx_now * 2 * hkv * d * 4 + Bt * (km.n_heads * d * 4) * 2
+
+    # one prefill chunk of PF tokens on fresh blocks
+    pf_bt = list(range(Bt * nbs, Bt * nbs + npf))
+    prompt = torch.randint(0, cfg.vocab, (PF,), generator=g).tolist()
+    km.prefill(prompt, pool, pf_bt, PF)
+    barrier()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    km.prefill(prompt, pool, pf_bt, PF)
+    p1.record(stream)
+    barrier()
+    pf_ms = p0.elapsed_time(p1)
+
+    t = torch.tensor([ms, e2e_ms, attn_ms, pf_ms], dtype=torch.float64, device=dev)
+    if ws > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms, e2e_ms, attn_ms, pf_ms = t.tolist()
+    hbm, _, peak_kind = measured_peaks()
+    wb = km.weight_bytes()
+    step_bytes = wb["layers"] + wb["lm_head"] + L_ * attn_bytes
+    achieved = attn_bytes / (attn_ms * 1e-3) / 1e9
+    res = dict(
+        metric="decode tok/s/GPU (generated tokens / decode step time, batch 64 at context 4096)",
+        value=Bt / (ms * 1e-3), unit="tok/s", n_gpus=ws, steps=args.steps,
+        warmup=max(args.warmup, 3), ms_per_step=ms, higher_is_better=True, scaling="strong",
+        vs_baseline=None, dtype="fp32 act / " + wl["quantize"] + " weights", data="synthetic",
+        config={"workload": args.workload, "model": cfg.name, "quantize": wl["quantize"],
+                "global_batch": Bt, "context": ctx, "block_size": bs,
+                "parallelism": f"tp{ws}", "kv_cache": "synthetic values (fp32)",
+                "decode_graph": graph,
+                "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB read per step on rank 0)"},
+        per_gpu={"value": Bt / (ms * 1e-3) / ws, "unit": "tok/s/GPU"},
+        decode_step={"bytes_rank0": step_bytes,
+                     "hbm_frac_of_" + peak_kind: step_bytes / (ms * 1e-3) / 1e9 / hbm},
+        prefill={"tokens": PF, "ms": pf_ms, "tok_s": PF / (pf_ms * 1e-3)},
+        e2e={"value": Bt / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": Bt * 8,
+             "d2h_bytes_per_step": Bt * 8},
+        roofline={"kernel": "fused decode attention (ksh_decode_attention), one layer",
+                  "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                  "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": None,
+                  "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": attn_ms},
+        gpu_launches=args.steps * (cfg.layers * 5 + 3),
+        clocks=clk.summary(),
+    )
+    if graph:
+        st.graph = None                 # release the captured NCCL calls before teardown
+    torch.cuda.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return res, rank
 
 
 def run_profile_lm_head(args, wl):
@@ -562,6 +734,8 @@ def main():
         return
     if args.impl == "reference":
         res, rank = run_reference(args, wl)
+    elif wl.get("tp"):
+        res, rank = run_tp(args, wl)
     else:
         res, rank = run_ours(args, wl)
     if rank == 0 and res is not None:

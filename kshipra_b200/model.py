@@ -38,6 +38,8 @@ from ._lib import call, ptr, stream_ptr
 from .chunked_prefill import AttentionWorkspace, paged_attention
 from .config import ModelConfig
 from .prefix_cache import BlockAllocator
+from .tensor_parallel import (down_col_range, gate_up_row_ranges, merge_argmax, o_col_range,
+                              qkv_row_ranges, take_cols, take_rows, tp_shape)
 from .quantization import (QuantizedLinear, QuantizedWeight, Workspace, linear_launch,
                            quantize_int4_per_group, quantize_int8_per_channel, swiglu_launch)
 
@@ -89,7 +91,12 @@ class KshipraModel:
 
     def __init__(self, hf_model=None, device: torch.device = None, quantize: Optional[str] = None,
                  *, config: Optional[ModelConfig] = None,
-                 state_dict: Optional[Dict[str, torch.Tensor]] = None, group_size: int = 128) -> None:
+                 state_dict: Optional[Dict[str, torch.Tensor]] = None, group_size: int = 128,
+                 tp: Optional[tuple] = None) -> None:
+        """``tp=(rank, world, group)`` builds rank's tensor-parallel shard: heads,
+        intermediate rows and lm_head vocabulary split over ``world`` ranks
+        (one process per GPU), row-parallel sums all-reduced over ``group``
+        (a torch.distributed NCCL group; None = the default group)."""
         if quantize not in (None, "int8", "int4"):
             raise ValueError(f"quantize must be None, 'int8' or 'int4', got {quantize!r}")
         if device is None or torch.device(device).type != "cuda":
@@ -109,13 +116,16 @@ class KshipraModel:
         self.cfg = config
         self.quantize = quantize
         self.group_size = group_size
-        self.n_heads = config.heads
-        self.n_kv_heads = config.kv_heads
+        self.tp_rank, self.tp_world, self.tp_group = (0, 1, None) if tp is None else tp
+        self.tp = tp_shape(config, self.tp_rank, self.tp_world,
+                           group_size if quantize == "int4" else None)
+        self.n_heads = self.tp.heads                 # per rank
+        self.n_kv_heads = self.tp.kv_heads
         self.head_dim = config.head_dim
         self.n_layers = config.layers
         self.vocab_size = config.vocab
         self.hidden = config.hidden
-        self.inter = config.intermediate
+        self.inter = self.tp.inter
         self.eps = float(config.rms_eps)
         self._rope_theta = float(config.rope_theta)
         self._rope = None
@@ -155,14 +165,34 @@ class KshipraModel:
                               group_size=qw.group_size, in_features_padded=qw.in_features_padded)
         return QuantizedLinear.from_quantized(sub, bias)
 
+    def _shard_rows(self, proj: _Proj, ranges) -> _Proj:
+        if self.tp_world == 1:
+            return proj
+        if proj.qw is not None:
+            return _Proj(take_rows(proj.qw, ranges), None, None, sum(b - a for a, b in ranges))
+        w = torch.cat([proj.w[a:b] for a, b in ranges]).contiguous()
+        return _Proj(None, w, None, w.shape[0])
+
+    def _shard_cols(self, proj: _Proj, c0: int, c1: int) -> _Proj:
+        if self.tp_world == 1:
+            return proj
+        if proj.qw is not None:
+            return _Proj(take_cols(proj.qw, c0, c1), None, None, proj.qw.original_shape[0])
+        return _Proj(None, proj.w[:, c0:c1].contiguous(), None, proj.w.shape[0])
+
     def _load(self, sd: Dict[str, torch.Tensor]) -> None:
         dev = self.device
         g = lambda k: sd[k].detach().to(dev, torch.float32)
         self.embed = g("model.embed_tokens.weight").contiguous()
-        self.lm_head = (self.embed if ("lm_head.weight" not in sd or self.cfg.tie_embeddings)
-                        else g("lm_head.weight").contiguous())
+        lm = (self.embed if ("lm_head.weight" not in sd or self.cfg.tie_embeddings)
+              else g("lm_head.weight").contiguous())
+        v0 = self.tp.vocab_start
+        self.lm_head = lm if self.tp_world == 1 else lm[v0:v0 + self.tp.vocab].contiguous()
         self.norm_w = g("model.norm.weight").contiguous()
         qs, kvs = self.cfg.q_size, self.cfg.kv_size
+        tpr = self.tp
+        qkv_rows = qkv_row_ranges(self.cfg, tpr)
+        gu_rows = gate_up_row_ranges(self.cfg, tpr)
         self.layers: List[_Layer] = []
         for i in range(self.n_layers):
             p = f"model.layers.{i}."
@@ -171,16 +201,25 @@ class KshipraModel:
             L.ln2 = g(p + "post_attention_layernorm.weight").contiguous()
             wq, wk, wv = g(p + "self_attn.q_proj.weight"), g(p + "self_attn.k_proj.weight"), g(
                 p + "self_attn.v_proj.weight")
-            L.qkv = self._pack(torch.cat([wq, wk, wv], dim=0))
+            L.qkv = self._shard_rows(self._pack(torch.cat([wq, wk, wv], dim=0)), qkv_rows)
             bq = sd.get(p + "self_attn.q_proj.bias")
             if bq is not None:
-                L.qkv.bias = torch.cat([g(p + "self_attn.q_proj.bias"), g(p + "self_attn.k_proj.bias"),
-                                        g(p + "self_attn.v_proj.bias")]).contiguous()
+                bias = torch.cat([g(p + "self_attn.q_proj.bias"), g(p + "self_attn.k_proj.bias"),
+                                  g(p + "self_attn.v_proj.bias")])
+                if self.tp_world > 1:
+                    bias = torch.cat([bias[a:b] for a, b in qkv_rows])
+                L.qkv.bias = bias.contiguous()
             del wq, wk, wv
-            L.o = self._pack(g(p + "self_attn.o_proj.weight"))
-            L.gate_up = self._pack(torch.cat([g(p + "mlp.gate_proj.weight"),
-                                              g(p + "mlp.up_proj.weight")], dim=0))
-            L.down = self._pack(g(p + "mlp.down_proj.weight"))
+            L.o = self._shard_cols(self._pack(g(p + "self_attn.o_proj.weight")),
+                                   *o_col_range(self.cfg, tpr))
+            L.gate_up = self._shard_rows(self._pack(torch.cat([g(p + "mlp.gate_proj.weight"),
+                                                               g(p + "mlp.up_proj.weight")], dim=0)),
+                                         gu_rows)
+            L.down = self._shard_cols(self._pack(g(p + "mlp.down_proj.weight")),
+                                      *down_col_range(self.cfg, tpr))
+            self.layers.append(L)
+            if self.tp_world > 1:
+                continue            # the per-projection drop-in views are single-GPU only
             b = L.qkv.bias
             L.q_proj = self._view(L.qkv, 0, qs, None if b is None else b[:qs])
             L.k_proj = self._view(L.qkv, qs, qs + kvs, None if b is None else b[qs:qs + kvs])
@@ -189,7 +228,6 @@ class KshipraModel:
             L.gate_proj = self._view(L.gate_up, 0, self.inter)
             L.up_proj = self._view(L.gate_up, self.inter, 2 * self.inter)
             L.down_proj = self._view(L.down, 0, self.hidden)
-            self.layers.append(L)
         torch.cuda.synchronize(dev)
 
     def weight_bytes(self) -> Dict[str, int]:
@@ -230,7 +268,8 @@ class KshipraModel:
         return dict(
             hidden=torch.empty((T, self.hidden), dtype=f, device=dev),
             xn=torch.empty((T, self.hidden), dtype=f, device=dev),
-            qkv=torch.empty((T, self.cfg.q_size + 2 * self.cfg.kv_size), dtype=f, device=dev),
+            qkv=torch.empty((T, (self.n_heads + 2 * self.n_kv_heads) * self.head_dim), dtype=f,
+                            device=dev),
             q=torch.empty((T, self.n_heads, self.head_dim), dtype=f, device=dev),
             attn=torch.empty((T, self.n_heads, self.head_dim), dtype=f, device=dev),
             h=torch.empty((T, self.inter), dtype=f, device=dev),
@@ -267,11 +306,20 @@ class KshipraModel:
                      ptr(q), ptr(pool), nb, L, i, bs, ptr(self.flags), s)
                 paged_attention(q, pool, i, block_tables, q_start, prefix_lens, max_q_len,
                                 max_total_len, attn, self.flags, ws=attn_ws)
-            linear_launch(attn.view(T, -1), Ly.o.qw, Ly.o.w, None, hid, residual=hid, ws=lin_ws)
+            # row-parallel o / down: rank 0 adds the residual, the others write
+            # their partial sums, and the all-reduce completes hidden on every rank
+            res = hid if self.tp_rank == 0 else None
+            linear_launch(attn.view(T, -1), Ly.o.qw, Ly.o.w, None, hid, residual=res, ws=lin_ws)
+            self._all_reduce(hid)
             swiglu_launch(hid, Ly.gate_up.qw, Ly.gate_up.w, self.inter, h, ws=lin_ws,
                           norm_w=Ly.ln2, eps=eps)
-            linear_launch(h, Ly.down.qw, Ly.down.w, None, hid, residual=hid, ws=lin_ws)
+            linear_launch(h, Ly.down.qw, Ly.down.w, None, hid, residual=res, ws=lin_ws)
+            self._all_reduce(hid)
         return hid
+
+    def _all_reduce(self, t: torch.Tensor) -> None:
+        if self.tp_world > 1:
+            torch.distributed.all_reduce(t, group=self.tp_group)
 
     def _lm_workspace(self, m: int) -> torch.Tensor:
         need = int(_lib.lib().ksh_lm_head_workspace_size(m, self.vocab_size))
@@ -284,9 +332,33 @@ class KshipraModel:
         m = x.shape[0]
         if ws is None:
             ws = self._lm_workspace(m)
-        call("ksh_lm_head_argmax", ptr(x), m, self.hidden, ptr(self.norm_w), self.eps,
-             ptr(self.lm_head), self.vocab_size, ptr(logits), ptr(tokens), ptr(ws), ws.numel(),
-             stream_ptr())
+        vl = self.tp.vocab
+        if self.tp_world > 1 and logits is None:
+            logits = self._tp_logits(m)
+        # the fused norm + GEMV + argmax takes up to 16 rows per launch
+        for r0 in range(0, m, 16):
+            r1 = min(m, r0 + 16)
+            lg = None if logits is None else logits[r0:r1]
+            call("ksh_lm_head_argmax", ptr(x[r0:r1]), r1 - r0, self.hidden, ptr(self.norm_w),
+                 self.eps, ptr(self.lm_head), vl, ptr(lg), ptr(tokens[r0:r1]), ptr(ws),
+                 ws.numel(), stream_ptr())
+        if self.tp_world > 1:
+            # vocabulary-parallel: every rank's (max logit, global index), then
+            # the first index of the overall maximum
+            val = logits[:m].gather(1, tokens.view(-1, 1)).view(-1)
+            idx = tokens + self.tp.vocab_start
+            vals = torch.empty((self.tp_world, m), dtype=val.dtype, device=val.device)
+            idxs = torch.empty((self.tp_world, m), dtype=idx.dtype, device=idx.device)
+            torch.distributed.all_gather_into_tensor(vals, val.contiguous(), group=self.tp_group)
+            torch.distributed.all_gather_into_tensor(idxs, idx.contiguous(), group=self.tp_group)
+            tokens.copy_(merge_argmax(vals, idxs))
+
+    def _tp_logits(self, m: int) -> torch.Tensor:
+        buf = getattr(self, "_tp_lg", None)
+        if buf is None or buf.shape[0] < m:
+            buf = torch.empty((m, self.tp.vocab), dtype=torch.float32, device=self.device)
+            self._tp_lg = buf
+        return buf[:m]
 
     # ------------------------------------------------------------------ #
     # reference API
@@ -311,9 +383,14 @@ class KshipraModel:
             acts = self._alloc_acts(L)
             xn = self._run_layers(acts, ids, pos, slots, bt, q_start, pl, 1, L, prefix_len + L,
                                   pool, self._lin_ws, self._attn_ws)
-            logits = torch.empty((L, self.vocab_size), dtype=torch.float32, device=dev)
+            vl = self.tp.vocab
+            logits = torch.empty((L, vl), dtype=torch.float32, device=dev)
             linear_launch(xn, None, self.lm_head, None, logits, ws=self._lin_ws,
                           norm_w=self.norm_w, eps=self.eps)
+            if self.tp_world > 1:           # vocabulary shards -> full rows
+                parts = torch.empty((self.tp_world, L, vl), dtype=torch.float32, device=dev)
+                torch.distributed.all_gather_into_tensor(parts, logits, group=self.tp_group)
+                logits = parts.permute(1, 0, 2).reshape(L, self.vocab_size)
             _check_flags(self.flags)
         return logits.view(1, L, self.vocab_size)
 
