@@ -40,7 +40,7 @@ namespace {
 using namespace tc;
 
 constexpr int kTK = 16;          // keys per tile
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;   // 8 warps: enough in flight per SM at one CTA per SM
 constexpr int kMaxCluster = 8;
 
 struct DecArgs {
@@ -83,6 +83,7 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
   constexpr int CK = CH * kTK;                  // keys per chunk (64 or 128)
   constexpr int KW = CK / 32;                   // score warps along keys (one key per lane)
   static_assert(CK % 32 == 0 && KW >= 1 && KW <= kThreads / 32, "score mapping");
+  static_assert((kThreads / (D / 4)) * G * D <= NST * kTK * D, "PV reduction fits the K ring");
   constexpr int HW = (kThreads / 32) / KW;      // score warps along heads
   constexpr int GH = (G + HW - 1) / HW;         // heads per score warp
   constexpr int KGS = kThreads / D4;            // PV key groups
@@ -413,7 +414,8 @@ int launch_dec(const CUtensorMap& map, const DecArgs& a, int64_t B, int cluster,
 int decode_attention_cluster(int64_t batch, int64_t hkv, int64_t max_total_len) {
   const int64_t items = batch * hkv;
   const int64_t tiles = (max_total_len + kTK - 1) / kTK;
-  int64_t c = (2LL * num_sms() + items - 1) / items;
+  // enough CTAs for about four per SM (the key range split over a cluster)
+  int64_t c = (4LL * num_sms() + items - 1) / items;
   c = std::min<int64_t>(c, std::max<int64_t>(1, tiles / 2));
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(c, kMaxCluster)));
 }
