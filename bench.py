@@ -634,6 +634,59 @@ def run_profile_lm_head(args, wl):
                       "algorithmic_bytes": cfg.vocab * cfg.hidden * 4 + cfg.hidden * 8}))
 
 
+def run_profile_decode_attention(args, wl):
+    """The tensor-parallel workload's roofline kernel alone, for an ncu
+    capture: one layer's block pool for ``batch`` sequences at ``context``
+    earlier positions (fp32 K/V, 2.2 GB for the 8B shape at TP1) and one
+    ksh_decode_attention call between cudaProfilerStart/Stop, after a
+    warm-up."""
+    from kshipra_b200 import _lib as L
+    from kshipra_b200.config import PRESETS
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = PRESETS[wl["preset"]]
+    Bt, ctx, bs = wl["batch"], wl["context"], wl["block"]
+    hq, hkv, d = cfg.heads, cfg.kv_heads, cfg.head_dim
+    nbs = (ctx + 1 + bs - 1) // bs
+    pool = torch.empty((Bt * nbs, 1, 2, hkv, bs, d), device=dev).uniform_(-1.0, 1.0)
+    bt = torch.arange(Bt * nbs, dtype=torch.int32, device=dev).view(Bt, nbs)
+    g = torch.Generator(device=dev).manual_seed(0)
+    qkv = torch.randn((Bt, (hq + 2 * hkv) * d), generator=g, device=dev)
+    pos = torch.full((Bt,), ctx, dtype=torch.int64, device=dev)
+    slots = torch.arange(Bt, dtype=torch.int64, device=dev) * nbs * bs + ctx
+    ang = torch.arange(ctx + 1, device=dev, dtype=torch.float32)[:, None] * 1e-3
+    rc, rs = torch.cos(ang.expand(-1, d // 2)).contiguous(), torch.sin(ang.expand(-1, d // 2)).contiguous()
+    out = torch.empty((Bt, hq, d), device=dev)
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    s = L.stream_ptr()
+
+    def run():
+        L.call("ksh_decode_attention", qkv.data_ptr(), Bt, hq, hkv, d, pos.data_ptr(),
+               slots.data_ptr(), rc.data_ptr(), rs.data_ptr(), rc.shape[0], pool.data_ptr(),
+               pool.shape[0], 1, 0, bs, bt.data_ptr(), nbs, ctx + 1, out.data_ptr(),
+               flags.data_ptr(), s)
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 10
+    torch.cuda.cudart().cudaProfilerStart()
+    run()
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    if int(flags.abs().sum()):
+        raise RuntimeError(f"decode attention raised flags {flags.tolist()}")
+    nbytes = Bt * (ctx + 1) * 2 * hkv * d * 4 + Bt * hq * d * 8
+    print(json.dumps({"profile": "decode_attention", "workload": args.workload,
+                      "algorithmic_bytes": nbytes, "ms_unprofiled": ms,
+                      "gb_s_unprofiled": nbytes / (ms * 1e-3) / 1e9}))
+
+
 def profiled_traffic(name):
     """DRAM bytes per launch recorded in profiles/<name>.md (line
     'traffic_bytes_per_launch: N', from ncu dram__bytes_read.sum +
@@ -717,7 +770,7 @@ def main():
                     help="run one request inside cudaProfilerStart/Stop (for ncu)")
     ap.add_argument("--trace", action="store_true",
                     help="with --profile: CUPTI trace of one request, per-kernel summary")
-    ap.add_argument("--profile-kernel", default=None, choices=["lm_head"],
+    ap.add_argument("--profile-kernel", default=None, choices=["lm_head", "decode_attention"],
                     help="with --profile: only this kernel on the workload's shape (small ncu case)")
     ap.add_argument("--micro-filter", default=None,
                     help="micro workload: comma list of scheme:M:KxN points to run")
@@ -728,6 +781,9 @@ def main():
     wl = WORKLOADS[args.workload]
     if args.profile and args.profile_kernel == "lm_head":
         run_profile_lm_head(args, wl)
+        return
+    if args.profile and args.profile_kernel == "decode_attention":
+        run_profile_decode_attention(args, wl)
         return
     if args.profile:
         run_profile(args, wl)

@@ -59,6 +59,12 @@ int ksh_set_gemv_resident(int enabled);
  * previous mode.  A tuning switch with no counterpart in the reference;
  * results agree with the CUDA-core path within fp32 rounding. */
 int ksh_set_gemv_tc(int mode);
+/* Key split of ksh_decode_attention: the number of CTAs (one thread-block
+ * cluster) that share a (sequence, kv head), 1..8; 0 or out of range restores
+ * the per-launch choice (waves of resident CTAs x keys per CTA).  Returns the
+ * previous setting.  A tuning switch with no counterpart in the reference;
+ * results agree across splits within fp32 rounding. */
+int ksh_set_decode_split(int clusters);
 
 /* ------------------------------------------------------------------------
  * Weight packing.  w: fp32 [n, k] row-major.

@@ -7,21 +7,25 @@
 //
 // One thread-block cluster per (sequence, kv head); its CTAs split the key
 // range (tiles of 16 positions) evenly at run time from the sequence's
-// current length:
+// current length.  Inside a CTA the warps specialise:
 //
-// * each CTA streams its K/V tiles with 1-D bulk copies (cp.async.bulk) into
-//   a ring of shared-memory stages guarded by mbarriers; the first stages are
+// * warp 0 streams the CTA's K/V tiles into a ring of shared-memory stages
+//   with TMA (full / empty mbarrier pair per stage); the first stages are
 //   requested BEFORE the programmatic-launch wait: those pool rows belong to
 //   earlier positions, written by kernels that have completed (every kernel
 //   of this library triggers its dependents only after its own wait), so the
 //   K/V fetch overlaps the q/k/v projection still running;
-// * after the wait each CTA rotates the g query heads of the group; the CTA
-//   holding the last tile also rotates k, writes k and v to the pool (for
-//   later steps) and patches its shared-memory copy of that row;
-// * per tile: scores (q . k) / sqrt(D), the causal bound, and the reference's
-//   online-softmax merge (running max with m_safe, exp, rescale);
-// * the CTAs' (m, l, acc) are merged in rank order through distributed shared
-//   memory by cluster rank 0, which writes the output.
+// * after the wait all warps rotate the g query heads of the group; the CTA
+//   holding the last tile also rotates k and writes k and v to the pool (for
+//   later steps);
+// * consumer warps 1..3 take whole tiles round-robin, each with its own
+//   online-softmax state: scores (q . k) / sqrt(D) with the causal bound, the
+//   reference's merge (running max with m_safe, exp, rescale) and P.V.  A
+//   tile needs no CTA-wide barrier, so tiles of different warps overlap; the
+//   warp holding the new token's tile patches that row in shared memory;
+// * the warps' (m, l, acc) are merged per CTA, and the CTAs' in rank order
+//   through distributed shared memory by cluster rank 0, which writes the
+//   output.
 //
 // Bounds: block ids outside [0, num_blocks) raise KSH_FLAG_BAD_BLOCK (those
 // keys are skipped); positions outside the RoPE table raise
@@ -39,9 +43,13 @@ namespace {
 
 using namespace tc;
 
-constexpr int kTK = 16;          // keys per tile
-constexpr int kThreads = 256;   // 8 warps: enough in flight per SM at one CTA per SM
+constexpr int kTK = 16;                          // keys per tile
+constexpr int kConsumers = 3;                    // consumer warps per CTA
+constexpr int kThreads = 32 * (kConsumers + 1);  // + the TMA producer warp
 constexpr int kMaxCluster = 8;
+constexpr int kRingBytes = 96 * 1024;            // two CTAs per SM
+
+int g_forced_split = 0;                          // 0: cluster size chosen per launch
 
 struct DecArgs {
   const float* qkv;          // [B, (hq + 2 hkv) * d]
@@ -58,52 +66,63 @@ struct DecArgs {
   float scale;
 };
 
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // Staged K / V tiles: 16 rows x D floats as D/32 TMA boxes of 16 rows x 128 B,
-// 128B-swizzled (16-byte chunk c of row r at chunk c ^ (r & 7)).  Float4
-// column d4 of row r:
+// 128B-swizzled (16-byte chunk c of row r at chunk c ^ (r & 7)).  Float offset
+// of float4 column d4 of row r:
 template <int D>
 __device__ __forceinline__ int tile_off(int r, int d4) {
   return (d4 >> 3) * (kTK * 32) + r * 32 + (((d4 & 7) ^ (r & 7)) << 2);
 }
 
-template <int D, int G, int NST>
-__global__ void __launch_bounds__(kThreads)
+template <int D, int G>
+struct DecLayout {
+  static constexpr int D4 = D / 4;
+  static constexpr int TILE_F = kTK * D;                 // floats per K (or V) tile
+  static constexpr int STAGE_F = 2 * TILE_F;             // K tile then V tile
+  // 6 stages (D 128) / 12 (D 64), a multiple of the consumer count: tile i
+  // sits in stage i % NST and belongs to consumer i % kConsumers, so each
+  // stage is only ever read by one consumer, which waits on it again only
+  // after releasing it -- its full barrier is never more than one phase
+  // behind that wait (with stages shared between consumers a fast consumer
+  // could meet the completed phase of the stage's fill before last, which
+  // has the same parity).
+  static constexpr int NST = kRingBytes / (STAGE_F * 4) / kConsumers * kConsumers;
+  static constexpr int QS = D + 4;                       // padded q row (odd heads, other banks)
+  static constexpr int GP = (G + 3) & ~3;                // padded probability row
+  static constexpr int PW = (kTK + 1) * GP;              // per-warp probabilities + corr row
+  static constexpr int RING_F = NST * STAGE_F;
+  static constexpr int Q_OFF = RING_F;
+  static constexpr int P_OFF = Q_OFF + G * QS;
+  static constexpr int BAR_OFF = P_OFF + kConsumers * PW; // floats, then 2 NST mbarriers
+  static constexpr size_t SMEM = (BAR_OFF + 2 * NST * 2) * 4 + 1024;
+  // after the main loop the ring holds the warps' states [kConsumers][G][D+4]
+  // and, on cluster rank 0, every rank's state [kMaxCluster][G][D+4]
+  static constexpr int WST_F = kConsumers * G * (D + 4);
+  static constexpr int PART_F = kMaxCluster * G * (D + 4);
+  static_assert(NST >= 2 * kConsumers && NST % kConsumers == 0, "stages per consumer");
+  static_assert(WST_F + PART_F <= RING_F, "merge areas fit the ring");
+  static_assert(BAR_OFF % 2 == 0 && Q_OFF % 4 == 0 && P_OFF % 4 == 0, "alignment");
+};
+
+template <int D, int G>
+__global__ void __launch_bounds__(kThreads, 2)
 decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
-  constexpr int D4 = D / 4;
-  constexpr int TILE_F = kTK * D;               // floats per staged K (or V) tile
-  constexpr int CH = NST / 2;                   // tiles per chunk (ring = 2 chunks)
-  constexpr int CK = CH * kTK;                  // keys per chunk (64 or 128)
-  constexpr int KW = CK / 32;                   // score warps along keys (one key per lane)
-  static_assert(CK % 32 == 0 && KW >= 1 && KW <= kThreads / 32, "score mapping");
-  static_assert((kThreads / (D / 4)) * G * D <= NST * kTK * D, "PV reduction fits the K ring");
-  constexpr int HW = (kThreads / 32) / KW;      // score warps along heads
-  constexpr int GH = (G + HW - 1) / HW;         // heads per score warp
-  constexpr int KGS = kThreads / D4;            // PV key groups
-  constexpr int KPG = CK / KGS;                 // keys per PV group and chunk
+  using Ly = DecLayout<D, G>;
+  constexpr int D4 = Ly::D4, TILE_F = Ly::TILE_F, STAGE_F = Ly::STAGE_F, NST = Ly::NST;
+  constexpr int QS = Ly::QS, GP = Ly::GP;
+  constexpr int GH = (G + 1) / 2;        // heads per lane in the score phase
+  constexpr int NACC = GH == 1 ? 4 : (GH == 2 ? 2 : 1);  // independent partial sums per head
   extern __shared__ __align__(128) float4 sm4[];
   // TMA 128B-swizzled destinations need 1024-byte alignment
   float* sm = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(sm4) + 1023) & ~uintptr_t(1023));
-  float* Kt = sm;                               // [NST][D/32][kTK][32], swizzled
-  float* Vt = Kt + NST * TILE_F;                // [NST][D/32][kTK][32], swizzled
-  float* Qs = Vt + NST * TILE_F;                // [G][D]
-  float* Ss = Qs + G * D;                       // [G][CK + 1]
-  float* corr_s = Ss + G * (CK + 1);            // [G]
-  float* ms = corr_s + G;                       // [G] running max
-  float* ls = ms + G;                           // [G] running sum
-  // offsets so far: 2*NST*TILE_F + G*D + G*CK + 4G floats, a multiple of 4
-  // [kMaxCluster][G][D + 4]: every rank's (m, l, pad, pad, acc), received by rank 0
-  float* part = ls + G;
-  uint64_t* full = reinterpret_cast<uint64_t*>(part + kMaxCluster * G * (D + 4));   // [NST]
+  float* ring = sm;                                   // [NST][K tile, V tile]
+  float* Qs = sm + Ly::Q_OFF;                         // [G][QS]
+  float* Ps = sm + Ly::P_OFF;                         // [kConsumers][kTK + 1][GP]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + Ly::BAR_OFF);   // [NST]
+  uint64_t* empty = full + NST;                                     // [NST]
   __shared__ int tile_ok[NST];
   __shared__ float newk[D], newv[D];
+  __shared__ int fail_s;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t rank = cluster_rank(), csize = cluster_size();
@@ -124,8 +143,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
   const int64_t head_rows = a.hkv * a.bs;                         // rows between K and V
   const int32_t* bt = a.block_tables + static_cast<int64_t>(b) * a.max_blocks;
 
-  // Thread 0 stages local tile i into stage i % NST with TMA (D/32 boxes for K
-  // and for V); an out-of-range block id marks the tile bad instead.
+  // The producer lane stages local tile i into stage i % NST (D/32 boxes for
+  // K and for V); an out-of-range block id marks the tile bad instead.
   auto issue = [&](int i) {
     const int s = i % NST;
     const int t = t_begin + i;
@@ -140,23 +159,24 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
     tile_ok[s] = 1;
     const int krow = static_cast<int>((((blk * a.num_layers + a.layer) * 2) * a.hkv + hk) * a.bs + off);
     const int vrow = krow + static_cast<int>(head_rows);
-    mbar_arrive_expect_tx(&full[s], 2u * TILE_F * 4u);
+    float* st = ring + s * STAGE_F;
+    mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(STAGE_F * 4));
 #pragma unroll
     for (int cb = 0; cb < D / 32; ++cb) {
-      tma_load_2d(Kt + s * TILE_F + cb * kTK * 32, &pool_map, &full[s], cb * 32, krow);
-      tma_load_2d(Vt + s * TILE_F + cb * kTK * 32, &pool_map, &full[s], cb * 32, vrow);
+      tma_load_2d(st + cb * kTK * 32, &pool_map, &full[s], cb * 32, krow);
+      tma_load_2d(st + TILE_F + cb * kTK * 32, &pool_map, &full[s], cb * 32, vrow);
     }
   };
 
   if (tid == 0) {
-    for (int s = 0; s < NST; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    fail_s = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&pool_map);
     for (int i = 0; i < ntl && i < NST; ++i) issue(i);
-  }
-  if (tid < G) {
-    ms[tid] = -INFINITY;
-    ls[tid] = 0.0f;
   }
 
   grid_dep_wait();
@@ -183,8 +203,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
     const float o1 = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(-x2, s));
     const float o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, s));
     if (h < G) {
-      Qs[h * D + j] = o1;
-      Qs[h * D + j + half] = o2;
+      Qs[h * QS + j] = o1;
+      Qs[h * QS + j + half] = o2;
     } else {
       newk[j] = o1;
       newk[j + half] = o2;
@@ -210,148 +230,208 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
     }
   }
 
-  // ---- chunks of CH tiles (CK = 64 keys) ----
-  // PV ownership: float4 column c4 over the KPG keys kg*KPG .. of each chunk,
-  // all G heads; partial sums stay per thread until the end.
-  const int c4 = tid % D4, kg = tid / D4;
+  const int cw = warp - 1;                       // consumer index (warp 0 produces)
   float4 acc[G];
 #pragma unroll
   for (int h = 0; h < G; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-  bool timed_out = false, bad_block = false;
-
-  for (int c0 = 0; c0 < ntl && !timed_out; c0 += CH) {
-    const int nt = min(CH, ntl - c0);
-    for (int i = c0; i < c0 + nt; ++i) {
-      if (!mbar_wait(&full[i % NST], (i / NST) & 1)) timed_out = true;
-      if (!tile_ok[i % NST]) bad_block = true;
-    }
-    if (timed_out) break;
-    if (owner && c0 + nt == ntl) {             // patch the new token's row
-      const int i = ntl - 1, s = i % NST;
-      const int rr = static_cast<int>(p) - (t_begin + i) * kTK;
-      for (int j = tid; j < D; j += kThreads) {
-        Kt[s * TILE_F + tile_off<D>(rr, j >> 2) + (j & 3)] = newk[j];
-        Vt[s * TILE_F + tile_off<D>(rr, j >> 2) + (j & 3)] = newv[j];
-      }
-      __syncthreads();
-    }
-    const int kbase = (t_begin + c0) * kTK;    // absolute position of chunk key 0
-    const int nk = nt * kTK;
-    // scores: warp (kh, hh): lane -> key kh*32 + lane, heads hh*GH ..; q read as broadcast
-    {
-      const int kh = warp % KW, hh = warp / KW;
-      const int j = kh * 32 + lane;
-      const int s = (c0 + (j >> 4)) % NST;
-      const bool valid = j < nk && kbase + j < total_c && tile_ok[s];
-      const float* kt = Kt + s * TILE_F;
-      const int r = j & (kTK - 1);
-      float dot[GH];
+  float m_run[GH], l_run[GH];
 #pragma unroll
-      for (int u = 0; u < GH; ++u) dot[u] = 0.0f;
+  for (int u = 0; u < GH; ++u) {
+    m_run[u] = -INFINITY;
+    l_run[u] = 0.0f;
+  }
+
+  if (warp == 0) {
+    // ---- producer: refill each stage once its consumer released it ----
+    if (lane == 0) {
+      for (int i = NST; i < ntl; ++i) {
+        if (!mbar_wait(&empty[i % NST], ((i / NST) - 1) & 1)) {
+          atomicOr(&fail_s, 1);
+          break;
+        }
+        issue(i);
+      }
+    }
+  } else {
+    // ---- consumers: warp cw takes tiles cw, cw + kConsumers, ... ----
+    const int r = lane & (kTK - 1), hg = lane >> 4;
+    float* P = Ps + cw * Ly::PW;
+    bool bad = false;
+    for (int i = cw; i < ntl; i += kConsumers) {
+      const int s = i % NST;
+      const bool arrived = mbar_wait(&full[s], (i / NST) & 1);
+      if (__any_sync(0xffffffffu, !arrived)) {   // warp-uniform exit (shuffles below)
+        if (lane == 0) atomicOr(&fail_s, 1);
+        break;
+      }
+      float* Kt = ring + s * STAGE_F;
+      float* Vt = Kt + TILE_F;
+      const bool ok = tile_ok[s] != 0;
+      bad |= !ok;
+      if (owner && i == ntl - 1) {               // the new token's row, possibly stale in the pool copy
+        const int rr = static_cast<int>(p) - (t_begin + i) * kTK;
+        for (int j = lane; j < D; j += 32) {
+          Kt[tile_off<D>(rr, j >> 2) + (j & 3)] = newk[j];
+          Vt[tile_off<D>(rr, j >> 2) + (j & 3)] = newv[j];
+        }
+        __syncwarp();
+      }
+      const bool valid = ok && (t_begin + i) * kTK + r < total_c;
+      // scores: lane -> key r, heads hg, hg + 2, ...
+      float dot[GH][NACC];
+#pragma unroll
+      for (int u = 0; u < GH; ++u)
+#pragma unroll
+        for (int e = 0; e < NACC; ++e) dot[u][e] = 0.0f;
 #pragma unroll
       for (int d4 = 0; d4 < D4; ++d4) {
-        const float4 kv = *reinterpret_cast<const float4*>(kt + tile_off<D>(r, d4));
+        const float4 kv = *reinterpret_cast<const float4*>(Kt + tile_off<D>(r, d4));
 #pragma unroll
         for (int u = 0; u < GH; ++u) {
-          const int h = hh * GH + u;
-          if (h < G) {
-            const float4 qv = reinterpret_cast<const float4*>(Qs + h * D)[d4];
-            dot[u] = fmaf(qv.x, kv.x, dot[u]);
-            dot[u] = fmaf(qv.y, kv.y, dot[u]);
-            dot[u] = fmaf(qv.z, kv.z, dot[u]);
-            dot[u] = fmaf(qv.w, kv.w, dot[u]);
+          const int h = hg + 2 * u;
+          if (G % 2 == 0 || h < G) {
+            const float4 qv = *reinterpret_cast<const float4*>(Qs + h * QS + 4 * d4);
+            float& dd = dot[u][d4 % NACC];
+            dd = fmaf(qv.x, kv.x, dd);
+            dd = fmaf(qv.y, kv.y, dd);
+            dd = fmaf(qv.z, kv.z, dd);
+            dd = fmaf(qv.w, kv.w, dd);
           }
         }
       }
+      // online softmax over the tile's 16 keys (the lanes of one half-warp)
 #pragma unroll
       for (int u = 0; u < GH; ++u) {
-        const int h = hh * GH + u;
-        if (h < G) Ss[h * (CK + 1) + j] = valid ? dot[u] * a.scale : -INFINITY;
-      }
-    }
-    __syncthreads();
-    // online softmax merge, one warp per head
-    for (int h = warp; h < G; h += kThreads / 32) {
-      float* srow = Ss + h * (CK + 1);
-      float mx = -INFINITY;
-      for (int j = lane; j < CK; j += 32) mx = fmaxf(mx, srow[j]);
-      mx = warp_max(mx);
-      const float m_old = ms[h];
-      const float m_new = fmaxf(m_old, mx);
-      const float m_safe = isinf(m_new) ? 0.0f : m_new;
-      float psum = 0.0f;
-      for (int j = lane; j < CK; j += 32) {
-        const float pj = expf(srow[j] - m_safe);
-        srow[j] = pj;
-        psum += pj;
-      }
-      psum = warp_sum(psum);
-      if (lane == 0) {
-        const float corr = expf(m_old - m_safe);
-        ls[h] = __fadd_rn(__fmul_rn(ls[h], corr), psum);
-        ms[h] = m_new;
-        corr_s[h] = corr;
-      }
-    }
-    __syncthreads();
-    // acc[h][c4] = acc * corr[h] + sum_{j in group} p[h][j] V[j][c4]
+        const int h = hg + 2 * u;
+        float sc = dot[u][0];
 #pragma unroll
-    for (int h = 0; h < G; ++h) {
-      const float crr = corr_s[h];
-      acc[h].x *= crr;
-      acc[h].y *= crr;
-      acc[h].z *= crr;
-      acc[h].w *= crr;
-    }
-#pragma unroll 4
-    for (int jj = 0; jj < KPG; ++jj) {
-      const int j = kg * KPG + jj;
-      if (j < nk) {
-        const int s = (c0 + (j >> 4)) % NST;
-        const float4 v =
-            *reinterpret_cast<const float4*>(Vt + s * TILE_F + tile_off<D>(j & (kTK - 1), c4));
+        for (int e = 1; e < NACC; ++e) sc += dot[u][e];
+        const float sv = (valid && h < G) ? sc * a.scale : -INFINITY;
+        float tmax = sv;
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+        const float m_new = fmaxf(m_run[u], tmax);
+        const float m_safe = isinf(m_new) ? 0.0f : m_new;
+        const float pj = expf(sv - m_safe);
+        float psum = pj;
+#pragma unroll
+        for (int o = 8; o >= 1; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+        const float corr = expf(m_run[u] - m_safe);
+        l_run[u] = __fadd_rn(__fmul_rn(l_run[u], corr), psum);
+        m_run[u] = m_new;
+        if (h < G) {
+          P[r * GP + h] = pj;
+          if (r == 0) P[kTK * GP + h] = corr;
+        }
+      }
+      __syncwarp();
+      // acc[h][c4] = acc * corr[h] + sum_keys p[h][key] V[key][c4]
+      {
+        float pr4[GP];
+#pragma unroll
+        for (int q = 0; q < GP / 4; ++q) {
+          const float4 t = reinterpret_cast<const float4*>(P + kTK * GP)[q];
+          pr4[4 * q] = t.x; pr4[4 * q + 1] = t.y; pr4[4 * q + 2] = t.z; pr4[4 * q + 3] = t.w;
+        }
 #pragma unroll
         for (int h = 0; h < G; ++h) {
-          const float pj = Ss[h * (CK + 1) + j];
-          acc[h].x = fmaf(pj, v.x, acc[h].x);
-          acc[h].y = fmaf(pj, v.y, acc[h].y);
-          acc[h].z = fmaf(pj, v.z, acc[h].z);
-          acc[h].w = fmaf(pj, v.w, acc[h].w);
+          acc[h].x *= pr4[h];
+          acc[h].y *= pr4[h];
+          acc[h].z *= pr4[h];
+          acc[h].w *= pr4[h];
+        }
+      }
+      constexpr int KSTEP = D == 128 ? 1 : 2;    // D 64: the half-warps take alternate keys
+      const int c4 = D == 128 ? lane : (lane & 15);
+      const int k0 = D == 128 ? 0 : (lane >> 4);
+#pragma unroll 4
+      for (int kk = k0; kk < kTK; kk += KSTEP) {
+        const float4 v = *reinterpret_cast<const float4*>(Vt + tile_off<D>(kk, c4));
+        float pk[GP];
+#pragma unroll
+        for (int q = 0; q < GP / 4; ++q) {
+          const float4 t = reinterpret_cast<const float4*>(P + kk * GP)[q];
+          pk[4 * q] = t.x; pk[4 * q + 1] = t.y; pk[4 * q + 2] = t.z; pk[4 * q + 3] = t.w;
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h) {
+          acc[h].x = fmaf(pk[h], v.x, acc[h].x);
+          acc[h].y = fmaf(pk[h], v.y, acc[h].y);
+          acc[h].z = fmaf(pk[h], v.z, acc[h].z);
+          acc[h].w = fmaf(pk[h], v.w, acc[h].w);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (D == 64) {
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        acc[h].x += __shfl_xor_sync(0xffffffffu, acc[h].x, 16);
+        acc[h].y += __shfl_xor_sync(0xffffffffu, acc[h].y, 16);
+        acc[h].z += __shfl_xor_sync(0xffffffffu, acc[h].z, 16);
+        acc[h].w += __shfl_xor_sync(0xffffffffu, acc[h].w, 16);
+      }
+    }
+    if (bad && lane == 0) atomicOr(&fail_s, 2);
+  }
+  __syncthreads();                               // every stage consumed: the ring is free
+  if (tid == 0) {
+    if (fail_s & 1) raise_flag(a.flags, KSH_FLAG_TIMEOUT);
+    if (fail_s & 2) raise_flag(a.flags, KSH_FLAG_BAD_BLOCK);
+  }
+
+  // ---- per-CTA merge of the consumer warps' states ----
+  float* wst = ring;                              // [kConsumers][G][D + 4]: m, l, pad, pad, acc
+  if (warp > 0) {
+    const int r = lane & (kTK - 1), hg = lane >> 4;
+    if (D == 128 || lane < 16) {                 // D 64: both half-warps hold the sum
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+        reinterpret_cast<float4*>(wst + (cw * G + h) * (D + 4) + 4)[lane] = acc[h];
+    }
+    if (r == 0) {
+#pragma unroll
+      for (int u = 0; u < GH; ++u) {
+        const int h = hg + 2 * u;
+        if (h < G) {
+          wst[(cw * G + h) * (D + 4)] = m_run[u];
+          wst[(cw * G + h) * (D + 4) + 1] = l_run[u];
         }
       }
     }
-    __syncthreads();                           // this chunk's stages are free
-    if (tid == 0)
-      for (int i = c0 + NST; i < min(c0 + NST + CH, ntl); ++i) issue(i);
   }
-  if (tid == 0) {
-    if (timed_out) raise_flag(a.flags, KSH_FLAG_TIMEOUT);
-    if (bad_block) raise_flag(a.flags, KSH_FLAG_BAD_BLOCK);
-  }
-
-  // ---- reduce the PV key groups (the K ring is idle now) and send this CTA's
-  // (m, l, acc) to cluster rank 0 with remote shared-memory stores ----
-  float* red = Kt;                              // [KGS][G][D]
-#pragma unroll
-  for (int h = 0; h < G; ++h)
-    reinterpret_cast<float4*>(red + (kg * G + h) * D)[c4] = acc[h];
   __syncthreads();
+  float* part = ring + Ly::WST_F;                 // [kMaxCluster][G][D + 4] on rank 0
+  if (csize > 1) cluster_sync();                  // every rank is done with its ring
   const uint32_t slot0 = smem_u32(part + static_cast<int>(rank) * G * (D + 4));
   const uint32_t dst = csize > 1 ? map_rank(slot0, 0u) : slot0;
   for (int w = tid; w < G * D4; w += kThreads) {
     const int h = w / D4, c = w - h * D4;
-    float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int g2 = 0; g2 < KGS; ++g2) {
-      const float4 v = reinterpret_cast<const float4*>(red + (g2 * G + h) * D)[c];
-      s4.x += v.x; s4.y += v.y; s4.z += v.z; s4.w += v.w;
+    float M = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < kConsumers; ++q) M = fmaxf(M, wst[(q * G + h) * (D + 4)]);
+    const float Ms = isinf(M) ? 0.0f : M;
+    float Lsum = 0.0f;
+    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int q = 0; q < kConsumers; ++q) {
+      const float* ws_ = wst + (q * G + h) * (D + 4);
+      const float wgt = expf(ws_[0] - Ms);
+      Lsum = fmaf(ws_[1], wgt, Lsum);
+      const float4 ar = reinterpret_cast<const float4*>(ws_ + 4)[c];
+      A.x = fmaf(ar.x, wgt, A.x);
+      A.y = fmaf(ar.y, wgt, A.y);
+      A.z = fmaf(ar.z, wgt, A.z);
+      A.w = fmaf(ar.w, wgt, A.w);
     }
-    st_cluster_f32x4(dst + static_cast<uint32_t>((h * (D + 4) + 4 + 4 * c) * 4), s4);
+    st_cluster_f32x4(dst + static_cast<uint32_t>((h * (D + 4) + 4 + 4 * c) * 4), A);
+    if (c == 0) {
+      st_cluster_f32(dst + static_cast<uint32_t>(h * (D + 4) * 4), M);
+      st_cluster_f32(dst + static_cast<uint32_t>((h * (D + 4) + 1) * 4), Lsum);
+    }
   }
-  if (tid < G) {
-    st_cluster_f32(dst + static_cast<uint32_t>(tid * (D + 4) * 4), ms[tid]);
-    st_cluster_f32(dst + static_cast<uint32_t>((tid * (D + 4) + 1) * 4), ls[tid]);
-  }
-  if (csize > 1) cluster_sync();              // all ranks' states have landed in rank 0
+  if (csize > 1) cluster_sync();                  // all ranks' states have landed in rank 0
   else __syncthreads();
   if (rank != 0) return;
   for (int w = tid; w < G * D4; w += kThreads) {
@@ -380,21 +460,60 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
   }
 }
 
+// Cluster size (key split) for a launch: the estimated time of
+// ceil(CTAs / resident CTAs) waves of (tiles per CTA + a ramp of two tiles),
+// minimised over 1..8, the smaller size on ties.
+template <class K>
+int choose_split(K kern, size_t smem, int64_t items, int64_t tiles, int* resident) {
+  int best = 1;
+  double best_cost = 0.0;
+  const int cmax = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(kMaxCluster, tiles / 2)));
+  for (int c = 1; c <= cmax; ++c) {
+    if (resident[c] == 0) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(c), 1, 1);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = static_cast<unsigned>(c);
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = std::max(1, num_sms() / c);
+      }
+      resident[c] = n;
+    }
+    const int64_t slots = static_cast<int64_t>(resident[c]) * c;
+    const int64_t waves = (items * c + slots - 1) / slots;
+    const double cost = static_cast<double>(waves) * (static_cast<double>((tiles + c - 1) / c) + 2.0);
+    if (c == 1 || cost < best_cost) {
+      best = c;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
 template <int D, int G>
-int launch_dec(const CUtensorMap& map, const DecArgs& a, int64_t B, int cluster,
+int launch_dec(const CUtensorMap& map, const DecArgs& a, int64_t B, int64_t max_total_len,
                cudaStream_t stream) {
-  constexpr int NST = D == 64 ? 16 : 8;           // two chunks of 128 / 64 keys
-  constexpr int CK = (NST / 2) * kTK;
-  const size_t smem = (2ull * NST * kTK * D + static_cast<size_t>(G) * D + G * (CK + 1) +
-                       3 * G + static_cast<size_t>(kMaxCluster) * G * (D + 4)) * 4 + NST * 8 +
-                      1024;
-  auto kern = decode_attn_kernel<D, G, NST>;
-  if (smem > 32 * 1024 && set_smem_optin(reinterpret_cast<const void*>(kern), smem) != KSH_OK)
-    return KSH_ERR_CUDA;
+  using Ly = DecLayout<D, G>;
+  auto kern = decode_attn_kernel<D, G>;
+  if (set_smem_optin(reinterpret_cast<const void*>(kern), Ly::SMEM) != KSH_OK) return KSH_ERR_CUDA;
+  const int64_t items = B * a.hkv;
+  const int64_t tiles = (max_total_len + kTK - 1) / kTK;
+  static int resident[kMaxCluster + 1] = {};     // resident clusters per cluster size
+  const int cluster = g_forced_split > 0 ? g_forced_split
+                                         : choose_split(kern, Ly::SMEM, items, tiles, resident);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(cluster), static_cast<unsigned>(B * a.hkv), 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(cluster), static_cast<unsigned>(items), 1);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = Ly::SMEM;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -410,16 +529,6 @@ int launch_dec(const CUtensorMap& map, const DecArgs& a, int64_t B, int cluster,
 }
 
 }  // namespace
-
-int decode_attention_cluster(int64_t batch, int64_t hkv, int64_t max_total_len) {
-  const int64_t items = batch * hkv;
-  const int64_t tiles = (max_total_len + kTK - 1) / kTK;
-  // enough CTAs for about four per SM (the key range split over a cluster)
-  int64_t c = (4LL * num_sms() + items - 1) / items;
-  c = std::min<int64_t>(c, std::max<int64_t>(1, tiles / 2));
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(c, kMaxCluster)));
-}
-
 }  // namespace ksh
 
 using namespace ksh;
@@ -461,7 +570,6 @@ extern "C" int ksh_decode_attention(const float* qkv, int64_t batch, int64_t hq,
   a.max_blocks = max_blocks;
   a.g = static_cast<int>(g);
   a.scale = static_cast<float>(1.0 / sqrt(static_cast<double>(d)));
-  const int cl = decode_attention_cluster(batch, hkv, max_total_len);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // the pool as a 2-D tensor of token rows (D floats each) for TMA
   const int64_t rows = num_blocks * num_layers * 2 * hkv * block_size;
@@ -472,9 +580,15 @@ extern "C" int ksh_decode_attention(const float* qkv, int64_t batch, int64_t hq,
                           CU_TENSOR_MAP_SWIZZLE_128B))
     return KSH_ERR_UNSUPPORTED;
 #define KSH_DEC(DD, GG) \
-  if (d == DD && g == GG) return launch_dec<DD, GG>(map, a, batch, cl, st);
+  if (d == DD && g == GG) return launch_dec<DD, GG>(map, a, batch, max_total_len, st);
   KSH_DEC(64, 1) KSH_DEC(64, 2) KSH_DEC(64, 4) KSH_DEC(64, 7) KSH_DEC(64, 8)
   KSH_DEC(128, 1) KSH_DEC(128, 2) KSH_DEC(128, 4) KSH_DEC(128, 8)
 #undef KSH_DEC
   return KSH_ERR_UNSUPPORTED;
+}
+
+extern "C" int ksh_set_decode_split(int clusters) {
+  const int prev = g_forced_split;
+  g_forced_split = clusters >= 1 && clusters <= kMaxCluster ? clusters : 0;
+  return prev;
 }

@@ -418,7 +418,7 @@ def test_fused_decode_attention_vs_oracle(D, hq, hkv, bs):
     from kshipra_b200 import _lib
     from kshipra_b200.model import rope_tables
     gen = torch.Generator().manual_seed(D + hq + bs)
-    positions = [0, 5, 15, 16, 100, 561, 1023]
+    positions = [0, 5, 15, 16, 100, 561, 1023, 3000]
     B = len(positions)
     L, layer = 2, 1
     maxb = (max(positions) + 1 + bs - 1) // bs + 1
@@ -427,19 +427,26 @@ def test_fused_decode_attention_vs_oracle(D, hq, hkv, bs):
     bt = perm[:B * maxb].view(B, maxb).to(torch.int32)
     pool = torch.randn((nb, L, 2, hkv, bs, D), generator=gen)
     qkv = torch.randn((B, (hq + 2 * hkv) * D), generator=gen)
-    rc, rs = rope_tables(D, 10000.0, 2048)
+    rc, rs = rope_tables(D, 10000.0, 4096)
     pos = torch.tensor(positions, dtype=torch.int64)
     slots = torch.tensor([int(bt[b, p // bs]) * bs + p % bs for b, p in enumerate(positions)])
     dev = [t.cuda() for t in (qkv, pos, slots, rc, rs, bt)]
     poolc = pool.cuda()
-    out = torch.empty((B, hq, D), device="cuda")
-    flags = torch.zeros(1, dtype=torch.int32, device="cuda")
-    _lib.call("ksh_decode_attention", dev[0].data_ptr(), B, hq, hkv, D, dev[1].data_ptr(),
-              dev[2].data_ptr(), dev[3].data_ptr(), dev[4].data_ptr(), 2048, poolc.data_ptr(),
-              nb, L, layer, bs, dev[5].data_ptr(), maxb, max(positions) + 1, out.data_ptr(),
-              flags.data_ptr(), _lib.stream_ptr())
-    assert int(flags.item()) == 0
-    out = out.cpu()
+    outs = {}
+    # every key split (CTAs per sequence and kv head), and the per-launch choice (0)
+    for split in (0, 1, 2, 3, 5, 8):
+        out = torch.empty((B, hq, D), device="cuda")
+        flags = torch.zeros(1, dtype=torch.int32, device="cuda")
+        prev = _lib.lib().ksh_set_decode_split(split)
+        try:
+            _lib.call("ksh_decode_attention", dev[0].data_ptr(), B, hq, hkv, D, dev[1].data_ptr(),
+                      dev[2].data_ptr(), dev[3].data_ptr(), dev[4].data_ptr(), 4096,
+                      poolc.data_ptr(), nb, L, layer, bs, dev[5].data_ptr(), maxb,
+                      max(positions) + 1, out.data_ptr(), flags.data_ptr(), _lib.stream_ptr())
+        finally:
+            _lib.lib().ksh_set_decode_split(prev)
+        assert int(flags.item()) == 0, split
+        outs[split] = out.cpu()
     pool_after = poolc.cpu()
     ref_pool = pool          # block tables are disjoint: one reference pool serves all
     qrs = []
@@ -459,5 +466,65 @@ def test_fused_decode_attention_vs_oracle(D, hq, hkv, bs):
         qr = qrs[b]
         ref = oa.chunked_attention(qr[0], ref_pool[:, layer, 0], ref_pool[:, layer, 1],
                                    bt[b].tolist(), p, 1, bs)
-        got = out[b].unsqueeze(1)
-        assert rel_l2(got.numpy(), ref.numpy()) < 1e-5, (b, p, rel_l2(got.numpy(), ref.numpy()))
+        for split, out in outs.items():
+            got = out[b].unsqueeze(1)
+            err = rel_l2(got.numpy(), ref.numpy())
+            assert err < 1e-5, (split, b, p, err)
+
+
+def test_fused_decode_attention_long_context_batch64():
+    """The 8B decode shape at full size: 64 sequences x 8 kv heads (g = 4,
+    D = 128) at ragged lengths near 4096 keys over a 2 GB block pool, at the
+    per-launch key split and at split 1 (the longest run of tiles per CTA).
+    No flag may be raised (every stage wait completes), and sampled
+    sequences match a float64 torch reference on the device."""
+    from kshipra_b200 import _lib
+    from kshipra_b200.model import rope_tables
+    B, hq, hkv, D, bs, ctx = 64, 32, 8, 128, 16, 4096
+    g = hq // hkv
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(11)
+    positions = torch.tensor([ctx - (b * 37) % 300 for b in range(B)], dtype=torch.int64)
+    maxb = (ctx + 1 + bs - 1) // bs
+    nb = B * maxb
+    bt = torch.randperm(nb, generator=torch.Generator().manual_seed(12)).view(B, maxb)
+    bt = bt.to(torch.int32).to(dev)
+    pool = torch.empty((nb, 1, 2, hkv, bs, D), device=dev).uniform_(-1.0, 1.0, generator=gen)
+    qkv = torch.randn((B, (hq + 2 * hkv) * D), generator=gen, device=dev)
+    rc, rs = (t.to(dev) for t in rope_tables(D, 500000.0, ctx + 1))
+    pos = positions.to(dev)
+    slots = torch.tensor([int(bt[b, int(p) // bs]) * bs + int(p) % bs
+                          for b, p in enumerate(positions)], dtype=torch.int64, device=dev)
+    outs = {}
+    for split in (0, 1):
+        out = torch.empty((B, hq, D), device=dev)
+        flags = torch.zeros(1, dtype=torch.int32, device=dev)
+        prev = _lib.lib().ksh_set_decode_split(split)
+        try:
+            _lib.call("ksh_decode_attention", qkv.data_ptr(), B, hq, hkv, D, pos.data_ptr(),
+                      slots.data_ptr(), rc.data_ptr(), rs.data_ptr(), rc.shape[0],
+                      pool.data_ptr(), nb, 1, 0, bs, bt.data_ptr(), maxb, ctx + 1,
+                      out.data_ptr(), flags.data_ptr(), _lib.stream_ptr())
+            torch.cuda.synchronize()
+        finally:
+            _lib.lib().ksh_set_decode_split(prev)
+        assert int(flags.item()) == 0, (split, int(flags.item()))
+        outs[split] = out
+    half = D // 2
+    for b in (0, 9, 33, 63):
+        p = int(positions[b])
+        q = qkv[b, :hq * D].view(hq, D).double()
+        c, s_ = rc[p].double(), rs[p].double()
+        qr = torch.cat([q[:, :half] * c - q[:, half:] * s_, q[:, half:] * c + q[:, :half] * s_], 1)
+        rows = [(int(bt[b, t // bs]), t % bs) for t in range(p + 1)]
+        blk = torch.tensor([r[0] for r in rows], device=dev)
+        off = torch.tensor([r[1] for r in rows], device=dev)
+        K = pool[blk, 0, 0, :, off].double()            # [keys, hkv, D] (new row written by the call)
+        V = pool[blk, 0, 1, :, off].double()
+        for split, out in outs.items():
+            for hk in range(hkv):
+                sc = qr[hk * g:(hk + 1) * g] @ K[:, hk].T / D ** 0.5
+                ref = torch.softmax(sc, -1) @ V[:, hk]
+                got = out[b, hk * g:(hk + 1) * g].double()
+                err = float((got - ref).norm() / ref.norm())
+                assert err < 1e-5, (split, b, hk, err)
