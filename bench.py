@@ -499,6 +499,18 @@ def run_tp(args, wl):
     for _ in range(max(args.warmup, 3)):
         step()
     barrier()
+    if args.profile:
+        # one decode step between cudaProfilerStart/Stop (ncu --profile-from-start off)
+        torch.cuda.cudart().cudaProfilerStart()
+        step()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        if graph:
+            st.graph = None
+        if ws > 1:
+            torch.distributed.destroy_process_group()
+        return {"profile": args.workload, "decode_graph": graph, "batch": Bt,
+                "launches_per_step": cfg.layers * 5 + 3}, rank
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
@@ -785,7 +797,7 @@ def main():
     if args.profile and args.profile_kernel == "decode_attention":
         run_profile_decode_attention(args, wl)
         return
-    if args.profile:
+    if args.profile and not wl.get("tp"):
         run_profile(args, wl)
         return
     if args.impl == "reference":
