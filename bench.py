@@ -161,11 +161,17 @@ def run_ours(args, wl):
         for _ in range(NEW - 2):
             st.graph.replay()
 
-    # warm-up (captures the graph)
+    # warm-up (captures the graph); the library's launch counter gives the
+    # kernels of one request: the prefill chunks and start, and the kernels
+    # recorded into the decode graph (one step)
+    n0 = L.lib().ksh_kernel_launches()
     first = km.prefill(prompt, alloc.pool, bt, C)
     st.start(first.view(1), [P])
+    per_prefill = L.lib().ksh_kernel_launches() - n0
     st.step_eager()
+    n0 = L.lib().ksh_kernel_launches()
     st.capture()
+    per_tok = L.lib().ksh_kernel_launches() - n0
     for _ in range(max(args.warmup, 3)):
         device_step()
     torch.cuda.synchronize()
@@ -263,14 +269,9 @@ def run_ours(args, wl):
         gpu_launches=None,
         clocks=clk.summary(),
     )
-    # this library's kernels per request, as counted in the ncu launch list
-    # (profiles/launches_qwen05b_int8.md): per prefill chunk 10 per layer + the
-    # embedding, one lm_head, per decode step 5 per layer + embedding, lm_head
-    # and the on-device greedy bookkeeping
-    n_layers = cfg.layers
-    per_chunk = n_layers * 10 + 1
-    per_tok = n_layers * 5 + 3
-    res["gpu_launches"] = args.steps * ((P + C - 1) // C * per_chunk + 1 + (NEW - 1) * per_tok)
+    # this library's kernels per request: prefill + start, then NEW - 1 graph
+    # replays of the decode step
+    res["gpu_launches"] = args.steps * (per_prefill + (NEW - 1) * per_tok)
     if rank == 0 and not args.no_cpu_baseline and ws == 1:
         res["cpu_baseline"] = cpu_baseline(wl, cfg, prompt, samples=1)
     if ws > 1:
@@ -487,7 +488,9 @@ def run_tp(args, wl):
             torch.distributed.barrier()
         torch.cuda.synchronize()
 
+    n0 = L.lib().ksh_kernel_launches()
     st.step_eager()
+    per_step = L.lib().ksh_kernel_launches() - n0               # this library's kernels per step
     graph = True
     try:
         st.capture()
@@ -510,7 +513,7 @@ def run_tp(args, wl):
         if ws > 1:
             torch.distributed.destroy_process_group()
         return {"profile": args.workload, "decode_graph": graph, "batch": Bt,
-                "launches_per_step": cfg.layers * 5 + 3}, rank
+                "launches_per_step": per_step}, rank
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
@@ -600,9 +603,11 @@ def run_tp(args, wl):
              "d2h_bytes_per_step": Bt * 8},
         roofline={"kernel": "fused decode attention (ksh_decode_attention), one layer",
                   "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                  "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": None,
+                  "frac": achieved / hbm, "peak_kind": peak_kind,
+                  "traffic": profiled_traffic("decode_attention_llama8b_b64_ctx4096") if ws == 1 else None,
+                  "traffic_source": "profiles/decode_attention_llama8b_b64_ctx4096.md (ncu, one launch, TP1)",
                   "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": attn_ms},
-        gpu_launches=args.steps * (cfg.layers * 5 + 3),
+        gpu_launches=args.steps * per_step,
         clocks=clk.summary(),
     )
     if graph:

@@ -65,6 +65,10 @@ int ksh_set_gemv_tc(int mode);
  * previous setting.  A tuning switch with no counterpart in the reference;
  * results agree across splits within fp32 rounding. */
 int ksh_set_decode_split(int clusters);
+/* Kernels this library has launched since it was loaded, counting those
+ * recorded into a CUDA graph under capture (a replay of that graph launches
+ * them again without counting). */
+uint64_t ksh_kernel_launches(void);
 
 /* ------------------------------------------------------------------------
  * Weight packing.  w: fp32 [n, k] row-major.

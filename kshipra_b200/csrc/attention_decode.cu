@@ -525,6 +525,7 @@ int launch_dec(const CUtensorMap& map, const DecArgs& a, int64_t B, int64_t max_
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, map, a);
+  if (e == cudaSuccess) count_launch();
   return e == cudaSuccess ? KSH_OK : record_cuda_error(e);
 }
 

@@ -76,6 +76,8 @@ bool pdl_enabled();
 bool prefetch_enabled();
 // Records e for ksh_last_cuda_error() and returns KSH_ERR_CUDA.
 int record_cuda_error(cudaError_t e);
+// Every successful kernel launch of the library (ksh_kernel_launches).
+void count_launch();
 
 template <typename... KArgs, typename... Args>
 inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
@@ -92,7 +94,9 @@ inline int launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
-  return e == cudaSuccess ? KSH_OK : record_cuda_error(e);
+  if (e != cudaSuccess) return record_cuda_error(e);
+  count_launch();
+  return KSH_OK;
 }
 
 int num_sms();

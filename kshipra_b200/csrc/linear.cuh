@@ -68,5 +68,13 @@ int set_gemv_tc_mode(int mode);
 int set_gemv_resident_enabled(int on);
 bool gemv_resident_enabled();
 int launch_gemm_simt(int wk, int epi, const LinArgs& a, cudaStream_t stream);
+// lm_head for 17..64 rows per launch (lm_head_gemm.cu): fused RMSNorm, fp32
+// GEMM reading the weight once, optional logits, optional greedy argmax.
+bool lm_gemm_ok(int64_t m, int64_t k, int64_t vocab, const float* x, const float* norm_w,
+                const float* w);
+int64_t lm_gemm_workspace_size(int64_t m, int64_t vocab);
+int launch_lm_gemm(const float* x, int64_t m, int64_t k, const float* norm_w, float eps,
+                   const float* w, int64_t vocab, float* logits, int64_t* tokens, char* ws,
+                   cudaStream_t stream);
 
 }  // namespace ksh

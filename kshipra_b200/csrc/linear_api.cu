@@ -195,9 +195,14 @@ argmax_rows_kernel(const float* __restrict__ logits, int64_t vocab, int64_t* out
 }  // namespace
 }  // namespace ksh
 
+// Rows above which the batch lm_head (one pass over the weight per 64 rows)
+// replaces the GEMV (one pass per 16 rows).
+constexpr int64_t kLmGemvMaxRows = 16;
+
 extern "C" int64_t ksh_lm_head_workspace_size(int64_t m, int64_t vocab) {
-  const int64_t mm = std::min<int64_t>(std::max<int64_t>(m, 1), 16);
-  return kLmHeadHeader + gemv_argmax_grid(vocab) * mm * 8;
+  const int64_t mm = std::min<int64_t>(std::max<int64_t>(m, 1), kLmGemvMaxRows);
+  const int64_t gemv = kLmHeadHeader + gemv_argmax_grid(vocab) * mm * 8;
+  return m > kLmGemvMaxRows ? std::max(gemv, lm_gemm_workspace_size(m, vocab)) : gemv;
 }
 
 extern "C" int ksh_argmax_rows(const float* logits, int64_t m, int64_t vocab, int64_t* out,
@@ -217,6 +222,22 @@ extern "C" int ksh_lm_head_argmax(const float* x, int64_t m, int64_t hidden,
   if (m == 0) return KSH_OK;
   LinArgs a = base(x, m, hidden, hidden, w, nullptr, 0, logits, vocab);
   set_norm(a, norm_w, norm_eps);
+  if (m > kLmGemvMaxRows && workspace &&
+      lm_gemm_ok(std::min<int64_t>(m, 64), hidden, vocab, x, norm_w, w)) {
+    // batch rows: 64 per launch, the weight read once per launch
+    const int64_t need = ksh_lm_head_workspace_size(m, vocab);
+    if (workspace_bytes < need) return KSH_ERR_WORKSPACE;
+    if (!aligned16(workspace)) return KSH_ERR_ALIGN;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    for (int64_t r0 = 0; r0 < m; r0 += 64) {
+      const int64_t rows = std::min<int64_t>(64, m - r0);
+      const int st = launch_lm_gemm(x + r0 * hidden, rows, hidden, norm_w, norm_eps, w, vocab,
+                                    logits ? logits + r0 * vocab : nullptr,
+                                    tokens ? tokens + r0 : nullptr, static_cast<char*>(workspace), s);
+      if (st != KSH_OK) return st;
+    }
+    return KSH_OK;
+  }
   if (tokens && gemv_ok(WK_F32, a)) {
     const int64_t need = ksh_lm_head_workspace_size(m, vocab);
     if (!workspace || workspace_bytes < need) return KSH_ERR_WORKSPACE;

@@ -580,6 +580,7 @@ int launch_tc(const LinArgs& a, char* ws, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mxh, mxl, mw, t);
+  if (e == cudaSuccess) count_launch();
   return e == cudaSuccess ? KSH_OK : record_cuda_error(e);
 }
 

@@ -1279,6 +1279,7 @@ int gv_launch(Kern kern, const GvPlan& p, size_t smem, cudaStream_t stream, cons
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mw, g);
+  if (e == cudaSuccess) count_launch();
   return e == cudaSuccess ? KSH_OK : record_cuda_error(e);
 }
 

@@ -39,6 +39,12 @@ int record_cuda_error(cudaError_t e) {
   return KSH_ERR_CUDA;
 }
 
+namespace {
+std::atomic<uint64_t> g_launches{0};
+}  // namespace
+
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 int num_sms() {
   static std::mutex mu;
   static std::unordered_map<int, int> cache;
@@ -159,3 +165,5 @@ extern "C" const char* ksh_status_string(int status) {
     default: return "unknown status";
   }
 }
+
+extern "C" uint64_t ksh_kernel_launches(void) { return ksh::g_launches.load(); }

@@ -335,13 +335,10 @@ class KshipraModel:
         vl = self.tp.vocab
         if self.tp_world > 1 and logits is None:
             logits = self._tp_logits(m)
-        # the fused norm + GEMV + argmax takes up to 16 rows per launch
-        for r0 in range(0, m, 16):
-            r1 = min(m, r0 + 16)
-            lg = None if logits is None else logits[r0:r1]
-            call("ksh_lm_head_argmax", ptr(x[r0:r1]), r1 - r0, self.hidden, ptr(self.norm_w),
-                 self.eps, ptr(self.lm_head), vl, ptr(lg), ptr(tokens[r0:r1]), ptr(ws),
-                 ws.numel(), stream_ptr())
+        # fused final norm + lm_head + argmax: a GEMV up to 16 rows, above that
+        # one pass over the weight per 64 rows
+        call("ksh_lm_head_argmax", ptr(x), m, self.hidden, ptr(self.norm_w), self.eps,
+             ptr(self.lm_head), vl, ptr(logits), ptr(tokens), ptr(ws), ws.numel(), stream_ptr())
         if self.tp_world > 1:
             # vocabulary-parallel: every rank's (max logit, global index), then
             # the first index of the overall maximum
@@ -481,9 +478,7 @@ class KshipraModel:
                                    device=dev)
             x = hid.index_select(0, rows)
             tok = torch.empty(len(want), dtype=torch.int64, device=dev)
-            for c0 in range(0, len(want), 16):       # the fused argmax takes up to 16 rows
-                c1 = min(c0 + 16, len(want))
-                self._lm_head_argmax(x[c0:c1], tok[c0:c1])
+            self._lm_head_argmax(x, tok)
             for i, t in zip(want, tok.tolist()):
                 out[i] = t
         _check_flags(self.flags)

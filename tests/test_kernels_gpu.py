@@ -337,18 +337,26 @@ def test_lm_head_argmax_first_index():
         assert float((lg.double() - ref).abs().max()) <= 1e-5 * float(ref.abs().max())
         assert tok.cpu().tolist() == torch.argmax(lg, dim=1).tolist()
         assert int(tok[0]) == 77
-        # argmax-only call (no logits) agrees
+        # argmax-only call (no logits) agrees, and a logits-only call
         tok2 = torch.empty(m, dtype=torch.int64, device="cuda")
-        if m <= 16:
-            _lib.call("ksh_lm_head_argmax", xc.data_ptr(), m, H, None, 0.0, wc.data_ptr(), V, None,
-                      tok2.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_ptr())
-            assert tok2.cpu().tolist() == tok.cpu().tolist()
+        _lib.call("ksh_lm_head_argmax", xc.data_ptr(), m, H, None, 0.0, wc.data_ptr(), V, None,
+                  tok2.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_ptr())
+        assert tok2.cpu().tolist() == tok.cpu().tolist()
+        if m > 16:
+            lg2 = torch.empty((m, V), device="cuda")
+            _lib.call("ksh_lm_head_argmax", xc.data_ptr(), m, H, None, 0.0, wc.data_ptr(), V,
+                      lg2.data_ptr(), None, ws.data_ptr(), ws.numel(), _lib.stream_ptr())
+            assert torch.equal(lg2.cpu(), lg)
 
 
-@pytest.mark.parametrize("m,H,V", [(8, 4096, 128256), (16, 2048, 32000), (5, 4096, 1000)])
+@pytest.mark.parametrize("m,H,V", [(8, 4096, 128256), (16, 2048, 32000), (5, 4096, 1000),
+                                   (17, 4096, 128256), (64, 4096, 128256), (100, 896, 1000),
+                                   (33, 900, 130)])
 def test_lm_head_argmax_tiled_x_stays_in_workspace(m, H, V):
     """Hidden sizes whose staged activations span several shared-memory tiles
-    (Llama-3-8B lm_head at batch 5-16): logits, first-index argmax, and no
+    (Llama-3-8B lm_head at batch 5-16), and the batch path above 16 rows
+    (64 rows per launch, ragged vocabulary tiles, a hidden size that is not a
+    multiple of the 32-float weight step): logits, first-index argmax, and no
     write past the workspace the size query asked for."""
     from kshipra_b200 import _lib
     gen = torch.Generator().manual_seed(m + H + V)
