@@ -45,7 +45,29 @@ WORKLOADS = {
                          prefill=2048, block=16, tp=True),
     "llama8b-int8": dict(preset="llama-3-8b", quantize="int8", batch=64, context=4096,
                          prefill=2048, block=16, tp=True),
+    # config 3: continuous batching of 32 concurrent requests (Poisson trace,
+    # prompts 256-2048, 128 new tokens each), INT4 0.5B, replicas over ranks
+    "qwen05b-int4-cb": dict(preset="qwen2.5-0.5b", quantize="int4", requests=32, rate=8.0,
+                            prompt_range=(256, 2048), new=128, block=16, budget=2048, seed=42,
+                            cb=True),
 }
+
+
+def poisson_trace(num_requests, rate, prompt_range, new_range, seed):
+    """(arrival_s, prompt_len, max_new_tokens) per request, from the same
+    sequence of draws as the reference's generate_poisson_traffic
+    (benchmarks/traffic.py:23-55): per request one exponential inter-arrival
+    gap, then the prompt length, then the new-token count, from one
+    random.Random(seed)."""
+    import random
+    rng = random.Random(seed)
+    t, out = 0.0, []
+    for _ in range(num_requests):
+        t += rng.expovariate(rate)
+        p = rng.randint(*prompt_range)
+        n = rng.randint(*new_range)
+        out.append((t, p, n))
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -334,6 +356,33 @@ def run_reference(args, wl):
     from kshipra_b200.config import PRESETS
     cfg = PRESETS[wl["preset"]]
     g = torch.Generator().manual_seed(0)
+    if wl.get("cb"):
+        # The reference serves one request at a time: the trace's time is the
+        # sum of its requests' times.  Sample one 256-token request (chunked
+        # prefill + 2 decode tokens) and extrapolate with the per-token
+        # prefill and decode costs over every prompt length of the trace.
+        trace = poisson_trace(wl["requests"], wl["rate"], wl["prompt_range"],
+                              (wl["new"], wl["new"]), wl["seed"])
+        sample = dict(wl, prompt=256, chunk=128)
+        prompt = torch.randint(0, cfg.vocab, (256,), generator=g).tolist()
+        cb = cpu_baseline(sample, cfg, prompt, samples=1)
+        t_total = sum(cb["prefill_s"] * p / 256 + n * cb["decode_s_per_token"] for _, p, n in trace)
+        gen = sum(n for _, _, n in trace)
+        value = gen / t_total
+        cb = dict(cb, value=value, sample=cb["sample"] + f"; trace of {len(trace)} requests "
+                  f"extrapolated per token ({t_total:.0f} s serial)")
+        res = dict(metric="decode tok/s/GPU (generated tokens / trace time, 32 concurrent requests)",
+                   value=value, unit="tok/s", n_gpus=ws, steps=args.steps, warmup=args.warmup,
+                   ms_per_step=t_total * 1e3, higher_is_better=True, scaling="weak",
+                   vs_baseline=None, dtype="fp32 act / " + wl["quantize"] + " weights",
+                   data="synthetic",
+                   config={"workload": args.workload, "model": cfg.name, "quantize": wl["quantize"],
+                           "requests": wl["requests"], "new_tokens_per_request": wl["new"],
+                           "parallelism": "cpu, one request at a time"},
+                   impl="reference", cpu_baseline=cb,
+                   e2e={"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0})
+        return res, rank
     prompt = torch.randint(0, cfg.vocab, (wl["prompt"],), generator=g).tolist()
     cb = cpu_baseline(wl, cfg, prompt, samples=max(1, min(args.steps, 2)))
     res = dict(metric="decode tok/s/GPU (generated tokens / request time incl. 512-token chunked prefill)",
@@ -619,6 +668,149 @@ def run_tp(args, wl):
     return res, rank
 
 
+def run_cb(args, wl):
+    """Config 3: continuous batching through ContinuousEngine with the real
+    batched forward (run_batch: mixed prefill chunks and decode tokens in one
+    varlen pass per iteration).
+
+    One step = the whole trace: 32 requests from the Poisson trace, all
+    admitted at the start so that they run concurrently (arrival order kept),
+    each prefilled in chunks out of a 2048-token iteration budget and decoded
+    for 128 tokens.  value = generated tokens / trace time.  The engine reads
+    every iteration's tokens back to the host, so each step is end to end by
+    construction.  Multi-GPU: one independent replica per rank (weak scaling)."""
+    from kshipra_b200 import _lib as L
+    from kshipra_b200.config import PRESETS
+    from kshipra_b200.continuous import ContinuousEngine
+    from kshipra_b200.model import KshipraModel
+    from kshipra_b200.prefix_cache import PrefixCache
+    from kshipra_b200.weights import synthetic_state_dict
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+    cfg = PRESETS[wl["preset"]]
+    sd = synthetic_state_dict(cfg, seed=0, device=dev)
+    km = KshipraModel(config=cfg, state_dict=sd, quantize=wl["quantize"], device=dev)
+    del sd
+    torch.cuda.empty_cache()
+    trace = poisson_trace(wl["requests"], wl["rate"], wl["prompt_range"], (wl["new"], wl["new"]),
+                          wl["seed"])
+    g = torch.Generator().manual_seed(rank)
+    prompts = [torch.randint(0, cfg.vocab, (p,), generator=g).tolist() for _, p, _ in trace]
+    bs = wl["block"]
+    nblocks = sum((p + n + bs - 1) // bs for _, p, n in trace) + 16
+
+    def run_trace():
+        cache = PrefixCache(nblocks, bs, cfg.layers, cfg.kv_heads, cfg.head_dim,
+                            dtype=torch.float32, device=dev)
+        eng = ContinuousEngine(cache, block_size=bs, max_batch_tokens=wl["budget"],
+                               itl_budget_s=wl["budget"] * 1e-3, t_tok_s=1e-3, model=km)
+        reqs = [eng.add_request(p, n) for p, (_, _, n) in zip(prompts, trace)]
+        t0 = time.monotonic()
+        for r in reqs:
+            r.arrival_time = t0
+        # token emission times, taken here: the engine's itl_times keep the
+        # reference's arithmetic (continuous.py:252-255), not intervals
+        seen = [0] * len(reqs)
+        last = [t0] * len(reqs)
+        ttft, itl, it_pf, it_dec = [], [], [], []
+        iters = 0
+        profiled = False
+        while not all(r.state.value == "finished" for r in reqs):
+            decode_only = all(r.state.value in ("running", "finished") for r in reqs)
+            if args.profile and decode_only and not profiled:
+                # one decode-only iteration between cudaProfilerStart/Stop
+                torch.cuda.synchronize()
+                torch.cuda.cudart().cudaProfilerStart()
+                eng.step()
+                torch.cuda.synchronize()
+                torch.cuda.cudart().cudaProfilerStop()
+                profiled = True
+            else:
+                eng.step()
+            iters += 1
+            now = time.monotonic()
+            (it_dec if decode_only else it_pf).append(now - max(last + [t0]))
+            for j, r in enumerate(reqs):
+                k = len(r.generated_tokens)
+                if k > seen[j]:
+                    (ttft if seen[j] == 0 else itl).append(now - last[j])
+                    seen[j], last[j] = k, now
+        return reqs, iters, sorted(ttft), sorted(itl), sorted(it_pf), sorted(it_dec)
+
+    profile = args.profile
+    args.profile = False
+    for _ in range(max(args.warmup, 3) if not profile else 1):
+        run_trace()
+    if profile:
+        args.profile = True
+        run_trace()
+        if ws > 1:
+            torch.distributed.destroy_process_group()
+        return {"profile": args.workload, "captured": "one decode-only engine iteration"}, rank
+
+    def barrier():
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = L.lib().ksh_kernel_launches()
+    with ClockSampler(local) as clk:
+        barrier()
+        w0 = time.perf_counter()
+        e0.record(stream)
+        for _ in range(args.steps):
+            reqs, iters, ttft, itl, it_pf, it_dec = run_trace()
+        e1.record(stream)
+        barrier()
+        wall = (time.perf_counter() - w0) / args.steps
+    launches = L.lib().ksh_kernel_launches() - n0
+    ms = e0.elapsed_time(e1) / args.steps
+    gen = sum(len(r.generated_tokens) for r in reqs)
+    t = torch.tensor([ms, wall * 1e3], dtype=torch.float64, device=dev)
+    if ws > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms, wall_ms = t.tolist()
+
+    def pct(v, q):
+        return v[min(len(v) - 1, int(q * len(v)))] * 1e3 if v else None
+
+    prompt_tokens = sum(p for _, p, _ in trace)
+    res = dict(
+        metric="decode tok/s/GPU (generated tokens / trace time, 32 concurrent requests)",
+        value=ws * gen / (ms * 1e-3), unit="tok/s", n_gpus=ws, steps=args.steps,
+        warmup=max(args.warmup, 3), ms_per_step=ms, higher_is_better=True, scaling="weak",
+        vs_baseline=None, dtype="fp32 act / " + wl["quantize"] + " weights", data="synthetic",
+        config={"workload": args.workload, "model": cfg.name, "quantize": wl["quantize"],
+                "requests": wl["requests"], "prompt_tokens": prompt_tokens,
+                "new_tokens_per_request": wl["new"], "arrival": "Poisson trace order, all admitted at t0",
+                "iteration_budget_tokens": wl["budget"], "block_size": bs,
+                "parallelism": f"replicas{ws}",
+                "l2": "inputs larger than L2 (weights + growing K/V per iteration)"},
+        per_gpu={"value": gen / (ms * 1e-3), "unit": "tok/s/GPU"},
+        engine={"iterations": iters, "ttft_ms_p50": pct(ttft, 0.5), "ttft_ms_p99": pct(ttft, 0.99),
+                "itl_ms_p50": pct(itl, 0.5), "itl_ms_p99": pct(itl, 0.99),
+                "prefill_iterations": len(it_pf), "prefill_iter_ms_p50": pct(it_pf, 0.5),
+                "decode_iterations": len(it_dec), "decode_iter_ms_p50": pct(it_dec, 0.5),
+                "decode_iterations_ms_total": sum(it_dec) * 1e3},
+        e2e={"value": ws * gen / (wall_ms * 1e-3), "unit": "tok/s",
+             "h2d_bytes_per_step": 8 * (prompt_tokens + gen), "d2h_bytes_per_step": 8 * (gen + iters)},
+        gpu_launches=launches,
+        clocks=clk.summary(),
+    )
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return res, rank
+
+
 def run_profile_lm_head(args, wl):
     """The roofline kernel alone, for an ncu capture of a small case: the
     workload's fp32 lm_head weight [vocab, hidden] (544 MB for the 0.5B shape)
@@ -802,13 +994,15 @@ def main():
     if args.profile and args.profile_kernel == "decode_attention":
         run_profile_decode_attention(args, wl)
         return
-    if args.profile and not wl.get("tp"):
+    if args.profile and not wl.get("tp") and not wl.get("cb"):
         run_profile(args, wl)
         return
     if args.impl == "reference":
         res, rank = run_reference(args, wl)
     elif wl.get("tp"):
         res, rank = run_tp(args, wl)
+    elif wl.get("cb"):
+        res, rank = run_cb(args, wl)
     else:
         res, rank = run_ours(args, wl)
     if rank == 0 and res is not None:
