@@ -50,6 +50,10 @@ WORKLOADS = {
     "qwen05b-int4-cb": dict(preset="qwen2.5-0.5b", quantize="int4", requests=32, rate=8.0,
                             prompt_range=(256, 2048), new=128, block=16, budget=2048, seed=42,
                             cb=True),
+    # microbench part 2: decode attention of 64 requests sharing a radix-cached
+    # 1024-token system prefix, plus 1-3072-token unique suffixes (8B heads)
+    "attn-prefix": dict(preset="llama-3-8b", requests=64, prefix=1024, suffix=(1, 3072), block=16,
+                        seed=0, attn=True),
 }
 
 
@@ -811,6 +815,152 @@ def run_cb(args, wl):
     return res, rank
 
 
+def run_attn_prefix(args, wl):
+    """Microbench part 2: one decode-attention layer (ksh_decode_attention:
+    RoPE, K/V write, paged GQA attention) for 64 requests whose block tables
+    share the 64 blocks of a 1024-token prefix.  The prefix is inserted once
+    into the RadixTree; each request matches it (the shared blocks) and pins
+    the node, then allocates blocks for its unique suffix and the new token.
+
+    value = logical K/V bytes (every request's keys, the shared prefix counted
+    per request) / launch time; the unique bytes (prefix counted once) are
+    reported beside it -- the prefix stays in L2 across the requests that
+    share it, so the logical rate can exceed the HBM peak."""
+    from kshipra_b200 import _lib as L
+    from kshipra_b200.config import PRESETS
+    from kshipra_b200.model import rope_tables
+    from kshipra_b200.prefix_cache import PrefixCache
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = PRESETS[wl["preset"]]
+    hq, hkv, d, bs = cfg.heads, cfg.kv_heads, cfg.head_dim, wl["block"]
+    R, P = wl["requests"], wl["prefix"]
+    g = torch.Generator().manual_seed(wl["seed"])
+    sfx = torch.randint(wl["suffix"][0], wl["suffix"][1] + 1, (R,), generator=g).tolist()
+    nblocks = P // bs + sum((s + 1 + bs - 1) // bs + 1 for s in sfx) + 8
+    cache = PrefixCache(nblocks, bs, 1, hkv, d, dtype=torch.float32, device=dev)
+    prefix = torch.randint(0, cfg.vocab, (P,), generator=g).tolist()
+    pblocks = cache.allocate_blocks(P // bs)
+    cache.tree.insert(prefix, pblocks, 0, cache.tree.root)
+    tables, positions = [], []
+    for s in sfx:
+        toks = prefix + torch.randint(0, cfg.vocab, (s,), generator=g).tolist()
+        blocks, matched, node = cache.tree.match(toks)
+        assert matched == P and blocks == pblocks
+        cache.tree.pin(node)
+        own = cache.allocate_blocks((len(toks) + 1 - matched + bs - 1) // bs)
+        tables.append(blocks + own)
+        positions.append(len(toks))                    # the new token's position
+    maxb = max(len(t) for t in tables)
+    bt = torch.full((R, maxb), -1, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    pool = cache.allocator.pool
+    pool.uniform_(-1.0, 1.0)
+    btd = bt.to(dev)
+    pos = torch.tensor(positions, dtype=torch.int64, device=dev)
+    slots = torch.tensor([tables[i][p // bs] * bs + p % bs for i, p in enumerate(positions)],
+                         dtype=torch.int64, device=dev)
+    qkv = torch.randn((R, (hq + 2 * hkv) * d), device=dev)
+    rc, rs = (t.to(dev) for t in rope_tables(d, cfg.rope_theta, max(positions) + 1))
+    out = torch.empty((R, hq, d), device=dev)
+    flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    s_ = L.stream_ptr()
+
+    def run():
+        L.call("ksh_decode_attention", qkv.data_ptr(), R, hq, hkv, d, pos.data_ptr(), slots.data_ptr(),
+               rc.data_ptr(), rs.data_ptr(), rc.shape[0], pool.data_ptr(), pool.shape[0], 1, 0, bs,
+               btd.data_ptr(), maxb, max(positions) + 1, out.data_ptr(), flags.data_ptr(), s_)
+    for _ in range(max(args.warmup, 3)):
+        run()
+    torch.cuda.synchronize()
+    if int(flags.item()):
+        raise RuntimeError(f"decode attention raised flags {int(flags.item())}")
+    n0 = L.lib().ksh_kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    row = 2 * hkv * d * 4                               # K and V of one token, all kv heads
+    logical = sum(p + 1 for p in positions) * row + R * hq * d * 8
+    unique = (P + sum(p + 1 - P for p in positions)) * row + R * hq * d * 8
+    hbm, _, peak_kind = measured_peaks()
+    ach = logical / (ms * 1e-3) / 1e9
+    res = dict(
+        metric="paged GQA decode attention, logical K/V GB/s (64 requests sharing a 1024-token prefix)",
+        value=ach, unit="GB/s", n_gpus=1, steps=args.steps, warmup=max(args.warmup, 3),
+        ms_per_step=ms, higher_is_better=True, scaling="weak", vs_baseline=None, dtype="fp32",
+        data="synthetic",
+        config={"workload": args.workload, "model_heads": f"{hq}/{hkv} x {d}", "requests": R,
+                "shared_prefix": P, "suffix_range": list(wl["suffix"]),
+                "suffix_total": sum(sfx), "block_size": bs,
+                "l2": "prefix shared through L2 by construction; the suffix K/V (%.2f GB) exceed L2"
+                      % ((unique - P * row) / 1e9)},
+        unique={"bytes": unique, "gb_s": unique / (ms * 1e-3) / 1e9,
+                "frac_of_" + peak_kind: unique / (ms * 1e-3) / 1e9 / hbm},
+        e2e={"value": ach, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        roofline={"kernel": "fused decode attention (ksh_decode_attention), one layer", "bound": "hbm",
+                  "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                  "peak_kind": peak_kind, "traffic": None, "algorithmic_bytes_per_launch": logical,
+                  "launch_ms": ms},
+        gpu_launches=int(L.lib().ksh_kernel_launches() - n0),
+        clocks=clk.summary(),
+    )
+    return res, 0
+
+
+def run_reference_attn(args, wl):
+    """Reference arm of the shared-prefix microbench: the oracle's restatement
+    of chunked_attention (chunked_prefill.py:93-140, chunk_len 1) on the host
+    cores, one request at a time as the reference runs it, over a sample of
+    the workload's requests (same prefix and suffix lengths), in logical
+    K/V GB/s."""
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return None, rank
+    from kshipra_b200.config import PRESETS
+    from oracle.attention import chunked_attention
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = PRESETS[wl["preset"]]
+    hq, hkv, d, bs = cfg.heads, cfg.kv_heads, cfg.head_dim, wl["block"]
+    R, P = wl["requests"], wl["prefix"]
+    g = torch.Generator().manual_seed(wl["seed"])
+    sfx = torch.randint(wl["suffix"][0], wl["suffix"][1] + 1, (R,), generator=g).tolist()
+    sample = sfx[:4]
+    nb = P // bs + max(sample) // bs + 2
+    kp = torch.rand((nb, hkv, bs, d)) * 2 - 1
+    vp = torch.rand((nb, hkv, bs, d)) * 2 - 1
+    row = 2 * hkv * d * 4
+    nbytes, t = 0, 0.0
+    for s_ in sample:
+        p = P + s_
+        q = torch.randn((hq, 1, d))
+        bt = list(range((p + 1 + bs - 1) // bs))
+        t0 = time.perf_counter()
+        chunked_attention(q, kp, vp, bt, p, 1, bs)
+        t += time.perf_counter() - t0
+        nbytes += (p + 1) * row
+    value = nbytes / t / 1e9
+    res = dict(metric="paged GQA decode attention, logical K/V GB/s (64 requests sharing a 1024-token prefix)",
+               value=value, unit="GB/s", n_gpus=ws, steps=args.steps, warmup=args.warmup,
+               ms_per_step=1e3 * t / len(sample) * R, higher_is_better=True, scaling="weak",
+               vs_baseline=None, dtype="fp32", data="synthetic",
+               config={"workload": args.workload, "parallelism": "cpu, one request at a time"},
+               impl="reference",
+               cpu_baseline={"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": f"oracle chunked_attention, {len(sample)} of the {R} requests "
+                                       f"(contexts {[P + x for x in sample]}), {threads} threads"},
+               e2e={"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+    return res, rank
+
+
 def run_profile_lm_head(args, wl):
     """The roofline kernel alone, for an ncu capture of a small case: the
     workload's fp32 lm_head weight [vocab, hidden] (544 MB for the 0.5B shape)
@@ -997,12 +1147,16 @@ def main():
     if args.profile and not wl.get("tp") and not wl.get("cb"):
         run_profile(args, wl)
         return
-    if args.impl == "reference":
+    if args.impl == "reference" and wl.get("attn"):
+        res, rank = run_reference_attn(args, wl)
+    elif args.impl == "reference":
         res, rank = run_reference(args, wl)
     elif wl.get("tp"):
         res, rank = run_tp(args, wl)
     elif wl.get("cb"):
         res, rank = run_cb(args, wl)
+    elif wl.get("attn"):
+        res, rank = run_attn_prefix(args, wl)
     else:
         res, rank = run_ours(args, wl)
     if rank == 0 and res is not None:

@@ -59,6 +59,11 @@ int ksh_set_gemv_resident(int enabled);
  * previous mode.  A tuning switch with no counterpart in the reference;
  * results agree with the CUDA-core path within fp32 rounding. */
 int ksh_set_gemv_tc(int mode);
+/* One-row INT4 linears through the dp4a kernel (exact int32 products of the
+ * nibbles with three 8-bit digits of x): 1 on (default), 0 off (the GEMV /
+ * tensor-core paths take them).  Returns the previous setting.  A tuning
+ * switch with no counterpart in the reference. */
+int ksh_set_gemv_dp4a(int enabled);
 /* Key split of ksh_decode_attention: the number of CTAs (one thread-block
  * cluster) that share a (sequence, kv head), 1..8; 0 or out of range restores
  * the per-launch choice (waves of resident CTAs x keys per CTA).  Returns the

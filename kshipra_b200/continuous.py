@@ -17,6 +17,14 @@ the reference's.  With ``model=KshipraModel`` the step runs the real batched
 forward: all scheduled prefill chunks and decode tokens of the iteration go
 through one varlen pass of the kernels; the chunk that completes a prompt
 yields its first token (as ``generate`` does), each decode step the next one.
+
+With a model the radix tree also saves work (the reference matches prefixes
+but recomputes them): a request's prefill starts after the whole blocks of
+its prompt that the tree already holds (the last prompt token is always
+computed, it yields the first output token), and once its prompt is
+prefilled the prompt's whole blocks are published into the tree, so later
+requests with the same prefix reuse them.  Published blocks belong to the
+tree (freed by eviction once no request pins them), not to the request.
 """
 
 from __future__ import annotations
@@ -99,7 +107,8 @@ class ContinuousEngine:
 
     def _admission_check(self, req: Request) -> bool:
         need = self._required_blocks(req)
-        matched, _, node = self.cache.tree.match(req.prompt_tokens)
+        toks = req.prompt_tokens if self.model is None else req.prompt_tokens[:-1]
+        matched, _, node = self.cache.tree.match(toks)
         h_evict = 0
         cur = node
         while cur is not None and cur.parent is not None:
@@ -134,7 +143,10 @@ class ContinuousEngine:
         return SchedulerOutput(decodes, prefills, len(decodes) + (c_max - left))
 
     def _init_sequence(self, req: Request) -> None:
-        matched, _, node = self.cache.tree.match(req.prompt_tokens)
+        # With a model the last prompt token is never taken from the tree: its
+        # position starts the prefill, in a block of the request's own.
+        toks = req.prompt_tokens if self.model is None else req.prompt_tokens[:-1]
+        matched, matched_len, node = self.cache.tree.match(toks)
         self.cache.tree.pin(node)
         req._pinned = node  # type: ignore[attr-defined]
         new = self.cache.allocate_blocks(max(0, self._required_blocks(req) - len(matched)))
@@ -144,6 +156,30 @@ class ContinuousEngine:
         if req.swapped_kv is not None:
             req.prefill_pos = len(req.prompt_tokens)
             self._swap_in(req)
+        elif self.model is not None:
+            req.prefill_pos = matched_len             # the tree's blocks hold these positions
+
+    def _publish_prompt(self, req: Request) -> None:
+        """Insert the whole blocks of a prefilled prompt into the radix tree.
+
+        The tree is matched again first: blocks another request published
+        meanwhile stay the tree's, this request's copies of them stay its own
+        (freed when it finishes), and only the remainder is inserted.  The
+        request's pin moves to the deepest node of its prompt."""
+        bsz = self.block_size
+        full = len(req.prompt_tokens) // bsz
+        if full == 0:
+            return
+        toks = req.prompt_tokens[:full * bsz]
+        _, have, node = self.cache.tree.match(toks)
+        if have < full * bsz:
+            given = req.block_table[have // bsz:full]
+            node = self.cache.tree.insert(toks, given, have, node)
+            gone = set(given)
+            req._own_blocks = [b for b in req._own_blocks if b not in gone]  # type: ignore[attr-defined]
+        self.cache.tree.pin(node)
+        self._unpin(req)
+        req._pinned = node  # type: ignore[attr-defined]
 
     # ---------------- preemption ----------------
 
@@ -157,8 +193,10 @@ class ContinuousEngine:
             host.copy_(pool.index_select(0, idx), non_blocking=pool.is_cuda)
             if pool.is_cuda:
                 torch.cuda.current_stream(pool.device).synchronize()
-            for b in victim.block_table:
+            # blocks the request took from (or gave to) the radix tree stay the tree's
+            for b in getattr(victim, "_own_blocks", victim.block_table):
                 self.cache.allocator.free(b)
+            victim._own_blocks = []  # type: ignore[attr-defined]
             victim.swapped_kv = host
             victim.block_table = []
         self._unpin(victim)
@@ -190,6 +228,8 @@ class ContinuousEngine:
             req.prefill_pos += c
             if req.prefill_pos >= len(req.prompt_tokens):
                 req.state = SeqState.RUNNING
+                if self.model is not None:
+                    self._publish_prompt(req)
                 if req.req_id in first:
                     self._emit(req, first[req.req_id], now)
                     if len(req.generated_tokens) >= req.max_new_tokens:

@@ -68,6 +68,10 @@ int set_gemv_tc_mode(int mode);
 int set_gemv_resident_enabled(int on);
 bool gemv_resident_enabled();
 int launch_gemm_simt(int wk, int epi, const LinArgs& a, cudaStream_t stream);
+// One-row INT4 linear with dp4a integer dot products (gemv_i4_dp4a.cu).
+bool gemv_i4_dp4a_eligible(int wk, int epi, const LinArgs& a);
+int launch_gemv_i4_dp4a(int epi, const LinArgs& a, cudaStream_t stream);
+int set_gemv_dp4a_mode(int mode);
 // lm_head for 17..64 rows per launch (lm_head_gemm.cu): fused RMSNorm, fp32
 // GEMM reading the weight once, optional logits, optional greedy argmax.
 bool lm_gemm_ok(int64_t m, int64_t k, int64_t vocab, const float* x, const float* norm_w,

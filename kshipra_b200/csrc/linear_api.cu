@@ -35,6 +35,7 @@ bool gemv_ok(int wk, const LinArgs& a) {
 
 int run_linear(int wk, int epi, LinArgs& a, void* ws, int64_t ws_bytes, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (gemv_i4_dp4a_eligible(wk, epi, a)) return launch_gemv_i4_dp4a(epi, a, s);
   if (a.m <= kGemvMaxM && gemv_tc_eligible(wk, epi, a)) return launch_gemv_tc(wk, epi, a, s);
   if (gemv_ok(wk, a)) return launch_gemv(wk, epi, a, s);
   if (a.m > kGemvMaxM) {
@@ -256,3 +257,5 @@ extern "C" int ksh_lm_head_argmax(const float* x, int64_t m, int64_t hidden,
   if (st != KSH_OK || !tokens) return st;
   return ksh_argmax_rows(logits, m, vocab, tokens, stream);
 }
+
+extern "C" int ksh_set_gemv_dp4a(int enabled) { return set_gemv_dp4a_mode(enabled); }

@@ -187,6 +187,7 @@ def test_tensor_core_decode_linear(scheme, m, K, N, I):
     xc, nc = x.cuda(), nw.cuda()
     modes = (2, 3)       # integer-MMA kernels, then the fp16-operand kernel
     prev = _lib.lib().ksh_set_gemv_tc(2)
+    prev_dp4a = _lib.lib().ksh_set_gemv_dp4a(0)     # one-row INT4 would take the dp4a kernel
     try:
         for mode in modes:
             _lib.lib().ksh_set_gemv_tc(mode)
@@ -205,6 +206,56 @@ def test_tensor_core_decode_linear(scheme, m, K, N, I):
                 assert err.max() <= 2e-5, (mode, err)
     finally:
         _lib.lib().ksh_set_gemv_tc(prev)
+        _lib.lib().ksh_set_gemv_dp4a(prev_dp4a)
+
+
+@pytest.mark.parametrize("g", [32, 64, 128])
+@pytest.mark.parametrize("K,N,I", [(896, 1152, 640), (912, 999, 328), (4096, 6144, 1536),
+                                   (14336, 512, 64)])
+def test_dp4a_one_row_int4_linear(g, K, N, I):
+    """One-row INT4 linears through the dp4a kernel against fp64 with the
+    dequantized weight: bias + residual, fused RMSNorm, SwiGLU; an odd row
+    count (the last row pair has one row), K not a multiple of the group."""
+    from kshipra_b200 import _lib
+    from kshipra_b200.quantization import linear_launch, quantize_int4_per_group, swiglu_launch
+    gen = torch.Generator().manual_seed(g + K + N)
+    x = torch.randn((1, K), generator=gen) * 3.0
+    x[0, ::7] *= 1e-3                          # entries of very different size in one vector
+    w = torch.randn((N, K), generator=gen) * 0.03
+    wgu = torch.randn((2 * I, K), generator=gen) * 0.03
+    res = torch.randn((1, N), generator=gen)
+    bias = torch.randn((N,), generator=gen)
+    nw = 1.0 + 0.2 * torch.randn((K,), generator=gen)
+    qw, qgu = quantize_int4_per_group(w.cuda(), g), quantize_int4_per_group(wgu.cuda(), g)
+    p, s, _ = oq.quantize_int4_per_group(w.numpy(), g)
+    wd = oq.dequantize_int4(p, s, K, g).astype(np.float64)
+    p, s, _ = oq.quantize_int4_per_group(wgu.numpy(), g)
+    gud = oq.dequantize_int4(p, s, K, g).astype(np.float64)
+    x64 = x.double().numpy()
+    xn64 = _rms_norm64(x.numpy(), nw.numpy())
+    y64 = x64 @ wd.T + bias.double().numpy() + res.double().numpy()
+    yn64 = xn64 @ wd.T
+    gu = xn64 @ gud.T
+    h64 = gu[:, :I] / (1 + np.exp(-gu[:, :I])) * gu[:, I:]
+    xc, nc = x.cuda(), nw.cuda()
+    prev = _lib.lib().ksh_set_gemv_dp4a(1)
+    try:
+        n0 = _lib.lib().ksh_kernel_launches()
+        y = res.clone().cuda()
+        linear_launch(xc, qw, None, bias.cuda(), y, residual=y)
+        assert _lib.lib().ksh_kernel_launches() - n0 == 1
+        err = np.abs(y.cpu().numpy() - y64).max() / np.abs(y64).max()
+        assert err <= 2e-6, err
+        yn = torch.empty((1, N), device="cuda")
+        linear_launch(xc, qw, None, None, yn, norm_w=nc)
+        err = np.abs(yn.cpu().numpy() - yn64).max() / np.abs(yn64).max()
+        assert err <= 2e-6, err
+        h = torch.empty((1, I), device="cuda")
+        swiglu_launch(xc, qgu, None, I, h, norm_w=nc)
+        err = np.abs(h.cpu().numpy() - h64).max() / max(np.abs(h64).max(), 1e-3)
+        assert err <= 2e-6, err
+    finally:
+        _lib.lib().ksh_set_gemv_dp4a(prev)
 
 
 def _run_attention_case(q, kp, vp, bt, P, C, B):
@@ -478,6 +529,68 @@ def test_fused_decode_attention_vs_oracle(D, hq, hkv, bs):
             got = out[b].unsqueeze(1)
             err = rel_l2(got.numpy(), ref.numpy())
             assert err < 1e-5, (split, b, p, err)
+
+
+def test_fused_decode_attention_shared_prefix_blocks():
+    """Block tables that share their first blocks (a radix-cached prefix, as
+    in the shared-prefix microbench): every sequence reads the same prefix
+    blocks and writes its new token into its own block; outputs match a
+    float64 torch reference of each sequence, at every key split."""
+    from kshipra_b200 import _lib
+    from kshipra_b200.model import rope_tables
+    hq, hkv, D, bs = 32, 8, 128, 16
+    g = hq // hkv
+    dev = torch.device("cuda")
+    gen = torch.Generator(device=dev).manual_seed(21)
+    prefix_blocks = [3, 9, 0, 14]                      # 64 shared prefix positions
+    suffix = [1, 37, 200]
+    tables, positions, nxt = [], [], 20
+    for s in suffix:
+        own = list(range(nxt, nxt + (s + 1 + bs - 1) // bs))
+        nxt += len(own)
+        tables.append(prefix_blocks + own)
+        positions.append(len(prefix_blocks) * bs + s)
+    nb = nxt + 2
+    maxb = max(len(t) for t in tables)
+    bt = torch.full((len(tables), maxb), -1, dtype=torch.int32)
+    for i, t in enumerate(tables):
+        bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    bt = bt.to(dev)
+    B = len(tables)
+    pool = torch.empty((nb, 1, 2, hkv, bs, D), device=dev).uniform_(-1.0, 1.0, generator=gen)
+    qkv = torch.randn((B, (hq + 2 * hkv) * D), generator=gen, device=dev)
+    rc, rs = (t.to(dev) for t in rope_tables(D, 500000.0, max(positions) + 1))
+    pos = torch.tensor(positions, dtype=torch.int64, device=dev)
+    slots = torch.tensor([tables[i][p // bs] * bs + p % bs for i, p in enumerate(positions)],
+                         dtype=torch.int64, device=dev)
+    prefix_before = pool[prefix_blocks].clone()
+    half = D // 2
+    for split in (0, 1, 4):
+        out = torch.empty((B, hq, D), device=dev)
+        flags = torch.zeros(1, dtype=torch.int32, device=dev)
+        prev = _lib.lib().ksh_set_decode_split(split)
+        try:
+            _lib.call("ksh_decode_attention", qkv.data_ptr(), B, hq, hkv, D, pos.data_ptr(),
+                      slots.data_ptr(), rc.data_ptr(), rs.data_ptr(), rc.shape[0], pool.data_ptr(),
+                      nb, 1, 0, bs, bt.data_ptr(), maxb, max(positions) + 1, out.data_ptr(),
+                      flags.data_ptr(), _lib.stream_ptr())
+            torch.cuda.synchronize()
+        finally:
+            _lib.lib().ksh_set_decode_split(prev)
+        assert int(flags.item()) == 0
+        assert torch.equal(pool[prefix_blocks], prefix_before)      # the shared blocks stay intact
+        for b, p in enumerate(positions):
+            q = qkv[b, :hq * D].view(hq, D).double()
+            c, s_ = rc[p].double(), rs[p].double()
+            qr = torch.cat([q[:, :half] * c - q[:, half:] * s_, q[:, half:] * c + q[:, :half] * s_], 1)
+            blk = torch.tensor([tables[b][t // bs] for t in range(p + 1)], device=dev)
+            off = torch.tensor([t % bs for t in range(p + 1)], device=dev)
+            K, V = pool[blk, 0, 0, :, off].double(), pool[blk, 0, 1, :, off].double()
+            for hk in range(hkv):
+                sc = qr[hk * g:(hk + 1) * g] @ K[:, hk].T / D ** 0.5
+                ref = torch.softmax(sc, -1) @ V[:, hk]
+                got = out[b, hk * g:(hk + 1) * g].double()
+                assert float((got - ref).norm() / ref.norm()) < 1e-5, (split, b, hk)
 
 
 def test_fused_decode_attention_long_context_batch64():

@@ -170,6 +170,48 @@ def test_continuous_engine_batched_forward_matches_generate(tiny_sd, scheme):
         assert r.generated_tokens == solo, (len(p), r.generated_tokens, solo)
 
 
+def test_continuous_engine_reuses_radix_prefix(tiny_sd):
+    """With a model the engine starts a prefill after the prompt blocks the
+    radix tree holds: request B shares 48 tokens (three blocks) with the
+    already finished request A, computes only its own tail, and still yields
+    the tokens of generate() run alone."""
+    from kshipra_b200.continuous import ContinuousEngine
+    from kshipra_b200.prefix_cache import PrefixCache
+    km = KshipraModel(config=TINY_LLAMA, state_dict=tiny_sd, quantize="int8")
+    cfg = km.cfg
+    g = torch.Generator().manual_seed(9)
+    shared = torch.randint(0, cfg.vocab, (48,), generator=g).tolist()
+    pa = shared + torch.randint(0, cfg.vocab, (21,), generator=g).tolist()
+    pb = shared + torch.randint(0, cfg.vocab, (10,), generator=g).tolist()
+    cache = PrefixCache(64, 16, cfg.layers, cfg.kv_heads, cfg.head_dim, dtype=torch.float32,
+                        device=torch.device("cuda"))
+    eng = ContinuousEngine(cache, block_size=16, max_batch_tokens=32, itl_budget_s=0.032,
+                           t_tok_s=1e-3, model=km)
+    computed = []
+    orig = km.run_batch
+
+    def counting(pool, seqs):
+        computed.append(sum(len(t) for t, _, _, _ in seqs))
+        return orig(pool, seqs)
+    km.run_batch = counting
+    ra = eng.add_request(pa, 5)
+    while ra not in eng.finished:
+        eng.step()
+    done_a = sum(computed)
+    rb = eng.add_request(pb, 5)
+    while rb not in eng.finished:
+        eng.step()
+    km.run_batch = orig
+    # A: its whole prompt + 4 decode tokens; B: only its 10-token tail + 4 decode tokens
+    assert done_a == len(pa) + 4
+    assert sum(computed) - done_a == 10 + 4
+    assert ra.generated_tokens == km.generate(pa, max_new_tokens=5, block_size=16)
+    assert rb.generated_tokens == km.generate(pb, max_new_tokens=5, block_size=16)
+    # the published blocks stay in the tree; the requests' own blocks went back
+    blocks, matched, _ = cache.tree.match(pa)
+    assert matched == 64 and len(blocks) == 4
+
+
 def test_run_batch_mixed_prefill_and_decode_vs_oracle(tiny_sd):
     """One pass holding a prefill chunk and decode steps of other sequences
     gives each sequence the oracle's next token."""
