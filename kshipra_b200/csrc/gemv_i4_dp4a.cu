@@ -27,6 +27,7 @@
 // which a decode GEMV streaming INT4 at HBM speed can afford.
 
 #include <math.h>
+#include <stdlib.h>
 
 #include <algorithm>
 
@@ -296,7 +297,11 @@ gemv_i4_dp4a_kernel(LinArgs a, int64_t items_per_cta) {
   }
 }
 
-int g_dp4a_mode = 1;     // 0 off, 1 on (one-row INT4 linears)
+// 0 off, 1 on (one-row INT4 linears); KSH_GEMV_DP4A=0 in the environment turns it off
+int g_dp4a_mode = [] {
+  const char* v = getenv("KSH_GEMV_DP4A");
+  return (v && *v) ? (atoi(v) != 0 ? 1 : 0) : 1;
+}();
 
 size_t dp4a_smem(const LinArgs& a) {
   return static_cast<size_t>(a.kp / 32) * 104 + static_cast<size_t>(kWarps) * 2 * (a.kp / a.g) * 2;
