@@ -389,9 +389,12 @@ Plan make_plan(int64_t num_seqs, int64_t hq, int64_t hkv, int64_t d, int64_t max
   p.nqt = static_cast<int>((std::max<int64_t>(max_q_len, 1) + p.qt - 1) / p.qt);
   p.items = num_seqs * hkv * p.nqt;
   const int64_t max_tiles = std::max<int64_t>(1, (max_total_len + kTK - 1) / kTK);
-  const int64_t target = 2LL * num_sms();
+  // Short chunks leave few items: split their keys finely (down to one
+  // 16-key tile per CTA) so that about four CTAs per SM share the work and
+  // each CTA's serial key walk stays short.
+  const int64_t target = 4LL * num_sms();
   int64_t ns = (target + p.items - 1) / p.items;
-  ns = std::min<int64_t>(ns, (max_tiles + 1) / 2);
+  ns = std::min<int64_t>(ns, max_tiles);
   ns = std::max<int64_t>(1, std::min<int64_t>(ns, 64));
   p.tps = static_cast<int>((max_tiles + ns - 1) / ns);
   p.nsplit = static_cast<int>((max_tiles + p.tps - 1) / p.tps);

@@ -33,6 +33,7 @@
 // mbarrier wait is bounded (KSH_FLAG_TIMEOUT).
 
 #include <math.h>
+#include <stdlib.h>
 
 #include <algorithm>
 
@@ -49,7 +50,12 @@ constexpr int kThreads = 32 * (kConsumers + 1);  // + the TMA producer warp
 constexpr int kMaxCluster = 8;
 constexpr int kRingBytes = 96 * 1024;            // two CTAs per SM
 
-int g_forced_split = 0;                          // 0: cluster size chosen per launch
+// 0: cluster size chosen per launch; KSH_DECODE_SPLIT=1..8 in the environment forces it
+int g_forced_split = [] {
+  const char* v = getenv("KSH_DECODE_SPLIT");
+  const int c = (v && *v) ? atoi(v) : 0;
+  return c >= 1 && c <= 8 ? c : 0;
+}();
 
 struct DecArgs {
   const float* qkv;          // [B, (hq + 2 hkv) * d]
