@@ -64,6 +64,12 @@ int ksh_set_gemv_tc(int mode);
  * tensor-core paths take them).  Returns the previous setting.  A tuning
  * switch with no counterpart in the reference. */
 int ksh_set_gemv_dp4a(int enabled);
+/* Quantized linears with 17..64 rows through the swap-AB tensor-core kernel
+ * (weight rows on the MMA's 128 lanes, token rows on its N side): 1 on
+ * (default), 0 off (the prefill GEMM takes them).  Returns the previous
+ * setting.  A tuning switch with no counterpart in the reference; results
+ * agree with the prefill GEMM within fp32 rounding. */
+int ksh_set_gemm_mid(int enabled);
 /* Key split of ksh_decode_attention: the number of CTAs (one thread-block
  * cluster) that share a (sequence, kv head), 1..8; 0 or out of range restores
  * the per-launch choice (waves of resident CTAs x keys per CTA).  Returns the

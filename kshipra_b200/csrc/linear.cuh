@@ -72,6 +72,10 @@ int launch_gemm_simt(int wk, int epi, const LinArgs& a, cudaStream_t stream);
 bool gemv_i4_dp4a_eligible(int wk, int epi, const LinArgs& a);
 int launch_gemv_i4_dp4a(int epi, const LinArgs& a, cudaStream_t stream);
 int set_gemv_dp4a_mode(int mode);
+// Batched decode linears, 17..64 rows, swap-AB on tcgen05 (qgemm_mid.cu).
+bool gemm_mid_eligible(int wk, int epi, const LinArgs& a, const void* ws, int64_t ws_bytes);
+int launch_gemm_mid(int wk, int epi, const LinArgs& a, void* ws, cudaStream_t stream);
+int set_gemm_mid_mode(int mode);
 // lm_head for 17..64 rows per launch (lm_head_gemm.cu): fused RMSNorm, fp32
 // GEMM reading the weight once, optional logits, optional greedy argmax.
 bool lm_gemm_ok(int64_t m, int64_t k, int64_t vocab, const float* x, const float* norm_w,

@@ -1,6 +1,7 @@
 // C ABI of the linear layers: shape checks and path selection.
 //
 //   m <= 16 and 16-byte aligned rows  -> vectorised GEMV (gemv.cu)
+//   17 <= m <= 64, quantized weights  -> swap-AB tcgen05 kernel (qgemm_mid.cu)
 //   m  > 16, tensor-core friendly     -> tcgen05 GEMM (qgemm_tc.cu)
 //   anything else                     -> generic CUDA-core GEMM (gemm_simt.cu)
 
@@ -38,6 +39,7 @@ int run_linear(int wk, int epi, LinArgs& a, void* ws, int64_t ws_bytes, void* st
   if (gemv_i4_dp4a_eligible(wk, epi, a)) return launch_gemv_i4_dp4a(epi, a, s);
   if (a.m <= kGemvMaxM && gemv_tc_eligible(wk, epi, a)) return launch_gemv_tc(wk, epi, a, s);
   if (gemv_ok(wk, a)) return launch_gemv(wk, epi, a, s);
+  if (a.m > kGemvMaxM && gemm_mid_eligible(wk, epi, a, ws, ws_bytes)) return launch_gemm_mid(wk, epi, a, ws, s);
   if (a.m > kGemvMaxM) {
     bool taken = false;
     int st = launch_gemm_tc(wk, epi, a, ws, ws_bytes, s, &taken);
@@ -259,3 +261,4 @@ extern "C" int ksh_lm_head_argmax(const float* x, int64_t m, int64_t hidden,
 }
 
 extern "C" int ksh_set_gemv_dp4a(int enabled) { return set_gemv_dp4a_mode(enabled); }
+extern "C" int ksh_set_gemm_mid(int enabled) { return set_gemm_mid_mode(enabled); }

@@ -416,6 +416,9 @@ __device__ __forceinline__ float norm_val(const float* xr, const float* norm_w, 
   return norm_w ? __fmul_rn(norm_w[j], __fmul_rn(v, inv)) : v;
 }
 
+// PERM stores each aligned 8-element chunk in the order [0,2,4,6,1,3,5,7] (the
+// order in which the INT4 decode kernels unpack nibbles).
+template <bool PERM>
 __global__ void __launch_bounds__(256)
 split_x_kernel(const float* __restrict__ x, int64_t k, __half* __restrict__ xh,
                __half* __restrict__ xl, float* __restrict__ inv_row,
@@ -465,8 +468,10 @@ split_x_kernel(const float* __restrict__ x, int64_t k, __half* __restrict__ xh,
   for (int64_t j = threadIdx.x; j < k; j += blockDim.x) {
     const float v = norm_val(xr, norm_w, inv, j) * sc;
     const __half h = __float2half_rn(v);
-    xh[r * k + j] = h;
-    xl[r * k + j] = __float2half_rn(v - __half2float(h));
+    // element e of a chunk goes to position (e & 1) * 4 + (e >> 1)
+    const int64_t pos = PERM && (j | 7) < k ? (j & ~int64_t{7}) + ((j & 1) << 2) + ((j & 7) >> 1) : j;
+    xh[r * k + pos] = h;
+    xl[r * k + pos] = __float2half_rn(v - __half2float(h));
   }
 }
 
@@ -528,8 +533,8 @@ int launch_tc(const LinArgs& a, char* ws, cudaStream_t stream) {
   __half* xh = reinterpret_cast<__half*>(ws + L.xh);
   __half* xl = reinterpret_cast<__half*>(ws + L.xl);
   float* inv = reinterpret_cast<float*>(ws + L.inv);
-  int st = launch(split_x_kernel, dim3(static_cast<unsigned>(a.m)), dim3(256), 0, stream, a.x, a.k,
-                  xh, xl, inv, a.norm_w, a.norm_eps);
+  int st = launch(split_x_kernel<false>, dim3(static_cast<unsigned>(a.m)), dim3(256), 0, stream, a.x,
+                  a.k, xh, xl, inv, a.norm_w, a.norm_eps);
   if (st != KSH_OK) return st;
   CUtensorMap mxh, mxl, mw;
   if (!make_tensor_map_2d(&mxh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, a.k, a.m, a.k * 2, BK, BM,
@@ -585,6 +590,19 @@ int launch_tc(const LinArgs& a, char* ws, cudaStream_t stream) {
 }
 
 }  // namespace
+
+int launch_split_x(const LinArgs& a, char* ws, bool perm, __half** xh, __half** xl, float** inv,
+                   cudaStream_t stream) {
+  const WsLayout L = ws_layout(a.m, a.k, a.n);
+  *xh = reinterpret_cast<__half*>(ws + L.xh);
+  *xl = reinterpret_cast<__half*>(ws + L.xl);
+  *inv = reinterpret_cast<float*>(ws + L.inv);
+  auto kern = perm ? split_x_kernel<true> : split_x_kernel<false>;
+  return launch(kern, dim3(static_cast<unsigned>(a.m)), dim3(256), 0, stream, a.x, a.k, *xh, *xl,
+                *inv, a.norm_w, a.norm_eps);
+}
+
+int64_t split_x_workspace_size(int64_t m, int64_t k) { return ws_layout(m, k, 0).total; }
 
 int64_t gemm_tc_workspace_size(int64_t m, int64_t k, int64_t n) {
   if (m <= 16) return 0;

@@ -209,6 +209,68 @@ def test_tensor_core_decode_linear(scheme, m, K, N, I):
         _lib.lib().ksh_set_gemv_dp4a(prev_dp4a)
 
 
+@pytest.mark.parametrize("scheme,g", [("int8", 0), ("int4", 128), ("int4", 64)])
+@pytest.mark.parametrize("m", [17, 31, 32, 33, 48, 64])
+@pytest.mark.parametrize("K,N,I", [(896, 1152, 640), (912, 1000, 328), (4096, 6144, 1536)])
+def test_mid_batch_linear(scheme, g, m, K, N, I):
+    """17..64 token rows through the swap-AB tensor-core kernel, then through
+    the prefill GEMM (kernel switched off), each against fp64 with the
+    dequantized weight: bias + residual, fused RMSNorm, SwiGLU; tiles that
+    overhang N, K not a multiple of the 64-wide stage, rows of very different
+    size."""
+    from kshipra_b200 import _lib
+    from kshipra_b200.quantization import (linear_launch, quantize_int4_per_group,
+                                           quantize_int8_per_channel, swiglu_launch)
+    gen = torch.Generator().manual_seed(m * 7 + K + N + g)
+    x = torch.randn((m, K), generator=gen)
+    x[0] *= 40.0
+    x[m - 1] *= 1e-3
+    w = torch.randn((N, K), generator=gen) * 0.03
+    wgu = torch.randn((2 * I, K), generator=gen) * 0.03
+    res = torch.randn((m, N), generator=gen)
+    bias = torch.randn((N,), generator=gen)
+    nw = 1.0 + 0.2 * torch.randn((K,), generator=gen)
+    if scheme == "int8":
+        qw, qgu = quantize_int8_per_channel(w.cuda()), quantize_int8_per_channel(wgu.cuda())
+        wd = oq.dequantize_int8(*oq.quantize_int8_per_channel(w.numpy()))
+        gud = oq.dequantize_int8(*oq.quantize_int8_per_channel(wgu.numpy()))
+    else:
+        qw, qgu = quantize_int4_per_group(w.cuda(), g), quantize_int4_per_group(wgu.cuda(), g)
+        p, s, _ = oq.quantize_int4_per_group(w.numpy(), g)
+        wd = oq.dequantize_int4(p, s, K, g)
+        p, s, _ = oq.quantize_int4_per_group(wgu.numpy(), g)
+        gud = oq.dequantize_int4(p, s, K, g)
+    wd, gud = wd.astype(np.float64), gud.astype(np.float64)
+    x64 = x.double().numpy()
+    xn64 = _rms_norm64(x.numpy(), nw.numpy())
+    y64 = x64 @ wd.T + bias.double().numpy() + res.double().numpy()
+    yn64 = xn64 @ wd.T
+    gu = xn64 @ gud.T
+    h64 = gu[:, :I] / (1 + np.exp(-gu[:, :I])) * gu[:, I:]
+    xc, nc = x.cuda(), nw.cuda()
+    prev = _lib.lib().ksh_set_gemm_mid(1)
+    try:
+        for mode in (1, 0):
+            _lib.lib().ksh_set_gemm_mid(mode)
+            for _ in range(2):
+                y = res.clone().cuda()
+                n0 = _lib.lib().ksh_kernel_launches()
+                linear_launch(xc, qw, None, bias.cuda(), y, residual=y)
+                assert _lib.lib().ksh_kernel_launches() - n0 == 2     # x split + GEMM
+                err = np.abs(y.cpu().numpy() - y64).max(axis=1) / np.abs(y64).max(axis=1)
+                assert err.max() <= 2e-5, (mode, err)
+                yn = torch.empty((m, N), device="cuda")
+                linear_launch(xc, qw, None, None, yn, norm_w=nc)
+                err = np.abs(yn.cpu().numpy() - yn64).max(axis=1) / np.abs(yn64).max(axis=1)
+                assert err.max() <= 2e-5, (mode, err)
+                h = torch.empty((m, I), device="cuda")
+                swiglu_launch(xc, qgu, None, I, h, norm_w=nc)
+                err = np.abs(h.cpu().numpy() - h64).max(axis=1) / np.maximum(np.abs(h64).max(axis=1), 1e-3)
+                assert err.max() <= 2e-5, (mode, err)
+    finally:
+        _lib.lib().ksh_set_gemm_mid(prev)
+
+
 @pytest.mark.parametrize("g", [32, 64, 128])
 @pytest.mark.parametrize("K,N,I", [(896, 1152, 640), (912, 999, 328), (4096, 6144, 1536),
                                    (14336, 512, 64)])
