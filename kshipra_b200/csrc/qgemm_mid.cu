@@ -9,8 +9,10 @@
 // * swap-AB: the MMA's M side (128 TMEM lanes) is 128 weight rows, its N side
 //   the MP = 32 or 64 token rows (zero-filled past m by TMA);
 // * x is split once per call (split_x_kernel: optional RMSNorm, a power-of-two
-//   row scale, x * 2^e = hi + lo in fp16) and both terms accumulate into the
-//   same fp32 TMEM columns, as in the prefill GEMM;
+//   row scale, x * 2^e = hi + lo in fp16); the lo tile sits right after the hi
+//   tile, so one MMA of N = 2 * MP takes both terms into separate TMEM columns
+//   (a tcgen05.mma costs about the same issue time at N = 64 as at 128, and
+//   the single issuing thread bounds this kernel);
 // * raw int8 / int4 weight tiles arrive by TMA and converter warps widen them
 //   to fp16 (exact) in the 128B-swizzled K-major layout; INT4 chunks are
 //   widened in the order [0,2,4,6,1,3,5,7], and split_x stores x in the same
@@ -18,7 +20,8 @@
 // * a CTA covers NT = 2 tiles of 128 weight rows, so each x stage fetched from
 //   L2 feeds 2 * NT * 4 MMAs;
 // * INT4 group scales are applied by promoting each group's TMEM partial into
-//   register accumulators (double-buffered TMEM, one FMA per token and row);
+//   register accumulators (double-buffered TMEM, an add and an FMA per token
+//   and row);
 //   INT8 accumulates the whole K-slice in TMEM and scales once;
 // * split-K over a thread-block cluster, reduced through distributed shared
 //   memory in rank order (deterministic); the epilogue applies the row factor
@@ -68,7 +71,8 @@ struct MidLayout {
   static constexpr int BAR_OFF = A_OFF + NA * ABUF;
   static constexpr int BYTES = BAR_OFF + 512;
   static constexpr int OUT_LD = NT * BW;                      // staged partials [MP][NT * BW]
-  static constexpr uint32_t TMEM_COLS = (WK == WK_I4 ? 2 : 1) * NT * MP;
+  // per tile and buffer: [hi-term columns: MP][lo-term columns: MP]
+  static constexpr uint32_t TMEM_COLS = (WK == WK_I4 ? 2 : 1) * NT * 2 * MP;
   static_assert(NS >= 3, "pipeline depth");
   static_assert(MP * OUT_LD * 4 <= RING, "staged partials reuse the TMA ring");
   static_assert(XT % 1024 == 0 && STAGE % 1024 == 0 && RAWT % 1024 == 0, "swizzle alignment");
@@ -215,7 +219,7 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
     grid_dep_wait();
     grid_dep_launch();
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(BW, MP);
+      constexpr uint32_t idesc = idesc_f16_f32(BW, 2 * MP);   // N: x hi rows, then lo rows
       for (int i = 0; i < ntl && !*abort_flag; ++i) {
         const int s = i % NS, b = i % NA;
         const int gl = i / ktpg, buf = WK == WK_I4 ? (gl & 1) : 0;
@@ -229,17 +233,18 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
           break;
         }
         tc_fence_after();
-        const uint32_t xh = smem_u32(xh_tile(s)), xl = smem_u32(xl_tile(s));
+        // The lo tile follows the hi tile in shared memory, so one B operand
+        // of 2 * MP rows carries both terms: one MMA per K step and tile
+        // (each tcgen05.mma costs about the same issue time up to N = 128).
+        const uint32_t xh = smem_u32(xh_tile(s));
 #pragma unroll
         for (int j = 0; j < NT; ++j) {
           const uint32_t ad = smem_u32(a_tile(b, j));
-          const uint32_t d = tmem + static_cast<uint32_t>((buf * NT + j) * MP);
+          const uint32_t d = tmem + static_cast<uint32_t>((buf * NT + j) * 2 * MP);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t adesc = desc_k_sw128(ad + kk * 32);
-            mma_f16(d, adesc, desc_k_sw128(xh + kk * 32), idesc, (first && kk == 0) ? 0u : 1u);
-            mma_f16(d, adesc, desc_k_sw128(xl + kk * 32), idesc, 1u);
-          }
+          for (int kk = 0; kk < BK / 16; ++kk)
+            mma_f16(d, desc_k_sw128(ad + kk * 32), desc_k_sw128(xh + kk * 32), idesc,
+                    (first && kk == 0) ? 0u : 1u);
         }
         mma_commit(&empty[s]);
         mma_commit(&afree[b]);
@@ -279,14 +284,15 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
       if (WK == WK_I4 && gl + 1 < ngl) sc_next = group_scale(gl + 1);
       if (!mbar_wait(&acc_full[buf], (gl >> 1) & 1)) return false;
       tc_fence_after();
-      const uint32_t taddr = tmem + static_cast<uint32_t>((buf * NT + j) * MP) + (static_cast<uint32_t>(q * 32) << 16);
+      const uint32_t taddr = tmem + static_cast<uint32_t>((buf * NT + j) * 2 * MP) + (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll
       for (int c = 0; c < MP / 32; ++c) {
-        float v[32];
-        tmem_ld_32x32b_x32(taddr + c * 32, v);
+        float vh[32], vl[32];
+        tmem_ld_32x32b_x32(taddr + c * 32, vh);
+        tmem_ld_32x32b_x32(taddr + MP + c * 32, vl);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) acc[c * 32 + e] = fmaf(v[e], sc, acc[c * 32 + e]);
+        for (int e = 0; e < 32; ++e) acc[c * 32 + e] = fmaf(vh[e] + vl[e], sc, acc[c * 32 + e]);
       }
       tc_fence_before();
       if (WK == WK_I4) mbar_arrive(&acc_empty[buf]);
