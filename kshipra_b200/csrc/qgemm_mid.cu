@@ -55,7 +55,13 @@ constexpr int BW = 128;                 // weight rows per tile (MMA M)
 constexpr int BK = 64;                  // K per stage (one 128-byte fp16 row)
 constexpr int NT = 2;                   // weight tiles per CTA
 constexpr int NA = 2;                   // fp16 weight operand buffers
-constexpr int kThreads = 64 + NT * 128; // TMA warp, MMA warp, NT * 4 converter warps
+// warp 0: TMA; warp 1: MMAs of tile 0; warps 2 .. 1 + 4 NT: converters;
+// warps 2 + 4 NT ..: MMAs of tiles 1 .. NT - 1 (one issuing thread per tile:
+// a single thread issues a tcgen05.mma only every ~70 cycles, slower than the
+// tensor core runs these N = 64 / 128 MMAs)
+constexpr int kConvWarp0 = 2;
+constexpr int kMmaWarpHi = kConvWarp0 + 4 * NT;
+constexpr int kThreads = 32 * (kMmaWarpHi + NT - 1);
 constexpr int kMaxSplits = 8;
 constexpr int A_TILE = BW * BK * 2;     // 16 KB
 
@@ -120,8 +126,7 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
   uint64_t* aready = empty + NS;       // [NA] fp16 weights written
   uint64_t* afree = aready + NA;       // [NA] MMAs done with them
   uint64_t* acc_full = afree + NA;     // [2]
-  uint64_t* acc_empty = acc_full + 2;  // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -139,16 +144,13 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + NT * 128);
+      mbar_init(&empty[s], NT + NT * 128);          // every tile's MMAs + the converters
     }
     for (int b = 0; b < NA; ++b) {
       mbar_init(&aready[b], NT * 128);
-      mbar_init(&afree[b], 1);
+      mbar_init(&afree[b], NT);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], NT * 128);
-    }
+    for (int b = 0; b < 2; ++b) mbar_init(&acc_full[b], NT);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&map_xh);
@@ -214,38 +216,38 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
       grid_dep_wait();
       grid_dep_launch();
     }
-  } else if (warp == 1) {
-    // ---------------- single-thread MMA issue ----------------
+  } else if (warp == 1 || warp >= kMmaWarpHi) {
+    // ---------------- MMA issue: one thread per weight tile ----------------
     grid_dep_wait();
     grid_dep_launch();
     if (lane == 0) {
+      const int j = warp == 1 ? 0 : warp - kMmaWarpHi + 1;
       constexpr uint32_t idesc = idesc_f16_f32(BW, 2 * MP);   // N: x hi rows, then lo rows
       for (int i = 0; i < ntl && !*abort_flag; ++i) {
         const int s = i % NS, b = i % NA;
         const int gl = i / ktpg, buf = WK == WK_I4 ? (gl & 1) : 0;
         const bool first = (i % ktpg) == 0;
-        if (WK == WK_I4 && first && gl >= 2 && !mbar_wait(&acc_empty[buf], ((gl >> 1) - 1) & 1)) {
-          *abort_flag = 1;
-          break;
-        }
-        if (!mbar_wait(&full[s], (i / NS) & 1) || !mbar_wait(&aready[b], (i / NA) & 1)) {
+        // One wait per stage: an mbarrier wait in this thread stalls until
+        // the MMAs it has in flight complete (a few hundred cycles), so it
+        // waits on the converters' barrier alone.  The converters arrive there
+        // after observing this stage's TMA barrier (x tiles landed) and, in
+        // program order, after promoting the group whose TMEM buffer this
+        // stage's MMAs overwrite (fenced with tcgen05.fence::before_thread_sync).
+        if (!mbar_wait(&aready[b], (i / NA) & 1)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
         // The lo tile follows the hi tile in shared memory, so one B operand
-        // of 2 * MP rows carries both terms: one MMA per K step and tile
-        // (each tcgen05.mma costs about the same issue time up to N = 128).
-        const uint32_t xh = smem_u32(xh_tile(s));
+        // of 2 * MP rows carries both terms: one MMA per K step.  A 32-byte
+        // step along K adds 2 to the descriptors' start-address field.
+        const uint64_t bdesc = desc_k_sw128(smem_u32(xh_tile(s)));
+        const uint64_t adesc = desc_k_sw128(smem_u32(a_tile(b, j)));
+        const uint32_t d = tmem + static_cast<uint32_t>((buf * NT + j) * 2 * MP);
+        mma_f16(d, adesc, bdesc, idesc, first ? 0u : 1u);
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          const uint32_t ad = smem_u32(a_tile(b, j));
-          const uint32_t d = tmem + static_cast<uint32_t>((buf * NT + j) * 2 * MP);
-#pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk)
-            mma_f16(d, desc_k_sw128(ad + kk * 32), desc_k_sw128(xh + kk * 32), idesc,
-                    (first && kk == 0) ? 0u : 1u);
-        }
+        for (int kk = 1; kk < BK / 16; ++kk)
+          mma_f16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, 1u);
         mma_commit(&empty[s]);
         mma_commit(&afree[b]);
         if ((i % ktpg) == ktpg - 1 || i == ntl - 1) mma_commit(&acc_full[buf]);
@@ -255,7 +257,7 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
     // ---------------- converters + promotion (NT * 128 threads) ----------------
     grid_dep_wait();
     grid_dep_launch();
-    const int cw = warp - 2;
+    const int cw = warp - kConvWarp0;
     const int j = cw >> 2;                          // weight tile of this warp
     const int q = warp & 3;                         // TMEM lane quadrant
     const int row = q * 32 + lane;                  // tile row = TMEM lane
@@ -294,8 +296,7 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
 #pragma unroll
         for (int e = 0; e < 32; ++e) acc[c * 32 + e] = fmaf(vh[e] + vl[e], sc, acc[c * 32 + e]);
       }
-      tc_fence_before();
-      if (WK == WK_I4) mbar_arrive(&acc_empty[buf]);
+      tc_fence_before();     // TMEM reads ordered before the next aready arrival
       return true;
     };
 
