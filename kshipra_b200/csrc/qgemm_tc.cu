@@ -423,39 +423,40 @@ __global__ void __launch_bounds__(256)
 split_x_kernel(const float* __restrict__ x, int64_t k, __half* __restrict__ xh,
                __half* __restrict__ xl, float* __restrict__ inv_row,
                const float* __restrict__ norm_w, float eps) {
-  __shared__ float red[8];
+  __shared__ float red[2][8];
   grid_dep_wait();
   grid_dep_launch();
   const int64_t r = blockIdx.x;
   const float* xr = x + r * k;
+  // One pass for both reductions: the sum of squares (RMSNorm) and the row
+  // maximum of |norm_w * x|, scaled by 1/rms afterwards.  That maximum can
+  // differ from the maximum of the normalised values by an ulp or two, which
+  // at most shifts the power-of-two exponent by one: the largest scaled value
+  // stays below 2^15 (1 + 2^-22), well inside fp16.
+  float ss = 0.0f, mx = 0.0f;
+  for (int64_t j = threadIdx.x; j < k; j += blockDim.x) {
+    const float v = xr[j];
+    ss = fmaf(v, v, ss);
+    mx = fmaxf(mx, fabsf(norm_w ? norm_w[j] * v : v));
+  }
+  ss = warp_sum(ss);
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = ss;
+    red[1][threadIdx.x >> 5] = mx;
+  }
+  __syncthreads();
+  ss = 0.0f;
+  mx = 0.0f;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) {     // fixed order
+    ss += red[0][w];
+    mx = fmaxf(mx, red[1][w]);
+  }
   float inv = 1.0f;
   if (norm_w) {
-    float ss = 0.0f;
-    for (int64_t j = threadIdx.x; j < k; j += blockDim.x) ss = fmaf(xr[j], xr[j], ss);
-    ss = warp_sum(ss);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
-      v = warp_sum(v);
-      if (threadIdx.x == 0) red[0] = v;
-    }
-    __syncthreads();
-    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(red[0], static_cast<float>(k)), eps)));
-    __syncthreads();
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(k)), eps)));
+    mx *= inv;
   }
-  float mx = 0.0f;
-  for (int64_t j = threadIdx.x; j < k; j += blockDim.x) mx = fmaxf(mx, fabsf(norm_val(xr, norm_w, inv, j)));
-  mx = warp_max(mx);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
-    v = warp_max(v);
-    if (threadIdx.x == 0) red[0] = v;
-  }
-  __syncthreads();
-  mx = red[0];
   int e = 0;
   if (mx > 0.0f && isfinite(mx)) {
     int ex;
