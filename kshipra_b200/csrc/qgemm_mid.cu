@@ -11,18 +11,20 @@
 // * x is split once per call (split_x_kernel: optional RMSNorm, a power-of-two
 //   row scale, x * 2^e = hi + lo in fp16); the lo tile sits right after the hi
 //   tile, so one MMA of N = 2 * MP takes both terms into separate TMEM columns
-//   (a tcgen05.mma costs about the same issue time at N = 64 as at 128, and
-//   the single issuing thread bounds this kernel);
+//   (an M = 128 tcgen05.mma takes max(~45, N / 2) cycles, so the wider MMA
+//   costs little more than one of the two narrow ones);
 // * raw int8 / int4 weight tiles arrive by TMA and converter warps widen them
 //   to fp16 (exact) in the 128B-swizzled K-major layout; INT4 chunks are
 //   widened in the order [0,2,4,6,1,3,5,7], and split_x stores x in the same
 //   order (a permutation of k applied to both operands leaves the sum as is);
 // * a CTA covers NT = 2 tiles of 128 weight rows, so each x stage fetched from
-//   L2 feeds 2 * NT * 4 MMAs;
+//   L2 feeds NT * 4 MMAs; each tile has its own MMA-issuing thread (one thread
+//   issues a tcgen05.mma only every ~70 cycles once commits are counted), and
+//   that thread waits once per stage, on the converters' barrier alone (an
+//   mbarrier wait stalls the issuing thread until its MMAs in flight finish);
 // * INT4 group scales are applied by promoting each group's TMEM partial into
 //   register accumulators (double-buffered TMEM, an add and an FMA per token
-//   and row);
-//   INT8 accumulates the whole K-slice in TMEM and scales once;
+//   and row); INT8 accumulates the whole K-slice in TMEM and scales once;
 // * split-K over a thread-block cluster, reduced through distributed shared
 //   memory in rank order (deterministic); the epilogue applies the row factor
 //   2^-e, bias, residual or SwiGLU (tile = 64 gate rows + the 64 matching up
