@@ -1,17 +1,22 @@
 """Benchmark of the quantized forward path (one JSON line on rank 0).
 
-Default workload (the configuration the headline metric is quoted on): the
-Qwen2.5-0.5B architecture, random-init N(0, 0.02), INT8 per-channel weights,
-fp32 activations; batch 1; a 512-token random prompt chunk-prefilled in
-128-token chunks, then 50 greedy decode tokens; KV block size 16.
+Default workload (the path that shards): the Llama-3-8B
+architecture, random-init N(0, 0.02), INT4 per-group (G = 128) weights, fp32
+activations; 64 sequences decoding at context 4096 (K/V of the earlier
+positions synthetic), KV block size 16, tensor parallel over the GPUs: heads,
+MLP rows and the vocabulary are split, with two NCCL all-reduces per layer.
+One step = one decode token for all 64 sequences (a CUDA-graph replay of
+embedding -> 32 layers -> vocabulary-parallel lm_head + argmax -> on-device
+position advance).  ``value`` = 64 tokens / step time for the whole job
+(strong scaling: the same batch over more GPUs); ``per_gpu`` = value / N.
+The 2048-token prefill chunk is timed beside it, and the Qwen2.5-0.5B INT8
+batch-1 request workload (config 2: 512-token prompt in 128-token chunks +
+50 greedy tokens; one independent replica per rank) is reported under
+``qwen05b_int8``.
 
-One step = one such request end to end (prefill + 50 tokens).  The metric is
-generated tokens per second per GPU, with the prefill inside the timed
-region as in the reference's own tok/s figure (new tokens / generate time);
-the decode-only rate is reported beside it.  Multi-GPU: the model shards
-nowhere at this size, so each rank runs an independent replica (weak
-scaling) and ``value`` sums the ranks' tokens over the slowest rank's time.
-
+``--workload`` selects the other configurations (``qwen05b-int8``,
+``qwen05b-int4``, ``qwen05b-int4-cb`` for config 3's continuous batching,
+``llama8b-int8``, ``attn-prefix`` and ``micro`` for config 5).
 ``--impl reference`` times the CPU oracle (a restatement of the reference's
 own algorithm, see oracle/) on this box's host cores instead.
 """
@@ -141,6 +146,26 @@ def measured_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+REPLICA_METRIC = ("decode tok/s, whole job (generated tokens of all ranks / request time incl. "
+                  "512-token chunked prefill; one request per GPU)")
+TP_METRIC = ("decode tok/s, whole job (Llama-3-8B shape, 64 sequences at context 4096, one "
+             "token each per step, tensor parallel over the GPUs; per GPU = value / n_gpus)")
+
+
+def replica_config(name, cfg, wl):
+    return {"workload": name, "model": cfg.name, "quantize": wl["quantize"], "batch_per_gpu": 1,
+            "prompt_len": wl["prompt"], "prefill_chunk": wl["chunk"], "new_tokens": wl["new"],
+            "block_size": wl["block"],
+            "l2": "inputs larger than L2 (every weight is streamed once per decode token)"}
+
+
+def tp_config(name, cfg, wl):
+    return {"workload": name, "model": cfg.name, "quantize": wl["quantize"],
+            "global_batch": wl["batch"], "context": wl["context"], "block_size": wl["block"],
+            "kv_cache": "fp32, synthetic values for the context positions",
+            "l2": "inputs larger than L2 (weights + K/V read per step: tens of GB, >> 126 MB)"}
+
+
 def dist_env():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -152,19 +177,98 @@ def dist_env():
 # our arm
 # ---------------------------------------------------------------------------
 
-def run_ours(args, wl):
+def time_linear_family(km, T, reps=20):
+    """The quantized linears of one decode step -- every layer's fused q/k/v
+    (RMSNorm folded in), o, gate/up + SwiGLU (RMSNorm folded in) and down --
+    at T token rows, captured in one CUDA graph (the same launches, with
+    programmatic dependent launch, as in the decode graph) and replayed.
+    Returns (ms per pass, algorithmic bytes per pass: packed weights + scales
+    + fp32 activations in and out)."""
+    from kshipra_b200.quantization import Workspace, linear_launch, swiglu_launch
+    acts = km._alloc_acts(T)
+    for t in acts.values():
+        t.normal_()
+    lws = Workspace()
+
+    def once():
+        for Ly in km.layers:
+            linear_launch(acts["hidden"], Ly.qkv.qw, Ly.qkv.w, Ly.qkv.bias, acts["qkv"], ws=lws,
+                          norm_w=Ly.ln1, eps=km.eps)
+            linear_launch(acts["attn"].view(T, -1), Ly.o.qw, Ly.o.w, None, acts["xn"], ws=lws)
+            swiglu_launch(acts["hidden"], Ly.gate_up.qw, Ly.gate_up.w, km.inter, acts["h"],
+                          ws=lws, norm_w=Ly.ln2, eps=km.eps)
+            linear_launch(acts["h"], Ly.down.qw, Ly.down.w, None, acts["xn"], ws=lws)
+    once()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            once()
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream()
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del g
+    H, I = km.hidden, km.inter
+    qkv = acts["qkv"].shape[1]
+    act = 4 * T * sum([H + qkv, acts["attn"].view(T, -1).shape[1] + H, H + I, I + H])
+    return ms, km.weight_bytes()["layers"] + km.n_layers * act
+
+
+def time_lm_head(km, T, reps=30):
+    """The fused final norm + fp32 lm_head + argmax at T rows, launched alone."""
+    from kshipra_b200 import _lib as L
+    dev = km.device
+    x = torch.randn((T, km.hidden), device=dev)
+    tok = torch.empty(T, dtype=torch.int64, device=dev)
+    ws = torch.empty(int(L.lib().ksh_lm_head_workspace_size(T, km.tp.vocab)), dtype=torch.uint8,
+                     device=dev)
+    lg = km._tp_logits(T) if km.tp_world > 1 else None
+    stream = torch.cuda.current_stream()
+
+    def once():
+        L.call("ksh_lm_head_argmax", x.data_ptr(), T, km.hidden, km.norm_w.data_ptr(), km.eps,
+               km.lm_head.data_ptr(), km.tp.vocab, None if lg is None else lg.data_ptr(),
+               tok.data_ptr(), ws.data_ptr(), ws.numel(), L.stream_ptr())
+    for _ in range(3):
+        once()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record(stream)
+    for _ in range(reps):
+        once()
+    r1.record(stream)
+    torch.cuda.synchronize()
+    ms = r0.elapsed_time(r1) / reps
+    nbytes = km.lm_head.numel() * 4 + T * km.hidden * 4 + (0 if lg is None else T * km.tp.vocab * 4)
+    return ms, nbytes
+
+
+def roofline_entry(kernel, nbytes, ms, hbm, peak_kind, traffic=None, source=None):
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    return {"kernel": kernel, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+            "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": traffic,
+            "traffic_source": source, "algorithmic_bytes_per_launch": nbytes, "launch_ms": ms}
+
+
+def measure_replica(args, wl, wl_name, ws, rank, local, dev, with_cpu_baseline):
+    """One Qwen2.5-0.5B request per rank (512-token chunked prefill + 50 greedy
+    tokens): an independent replica per rank, no data-path collective.  The
+    caller owns the process group."""
     from kshipra_b200.config import PRESETS
     from kshipra_b200.model import KshipraModel, DecodeState
     from kshipra_b200.weights import synthetic_state_dict
     import kshipra_b200._lib as L
 
-    ws, rank, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if ws > 1:
-        import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                             device_id=dev)
     cfg = PRESETS[wl["preset"]]
     sd = synthetic_state_dict(cfg, seed=0, device=dev)
     km = KshipraModel(config=cfg, state_dict=sd, quantize=wl["quantize"], device=dev)
@@ -244,24 +348,11 @@ def run_ours(args, wl):
     e2e_ms = a0.elapsed_time(a1) / args.steps
     assert out == tokens, "public API and device loop disagree"
 
-    # dominant kernel: the fp32 lm_head GEMV + argmax, timed alone
+    # the dominant kernel family of a decode token, the quantized linears,
+    # timed in graph replay; the lm_head (the largest single launch) beside it
     hbm, _, peak_kind = measured_peaks()
-    x = torch.randn((1, cfg.hidden), device=dev)
-    tok = torch.empty(1, dtype=torch.int64, device=dev)
-    lm_ws = torch.zeros(int(L.lib().ksh_lm_head_workspace_size(1, cfg.vocab)), dtype=torch.uint8,
-                        device=dev)
-    for _ in range(5):
-        km._lm_head_argmax(x, tok, ws=lm_ws)
-    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    R = 50
-    r0.record(stream)
-    for _ in range(R):
-        km._lm_head_argmax(x, tok, ws=lm_ws)
-    r1.record(stream)
-    torch.cuda.synchronize()
-    lm_ms = r0.elapsed_time(r1) / R
-    lm_bytes = cfg.vocab * cfg.hidden * 4 + cfg.hidden * 4
-    achieved = lm_bytes / (lm_ms * 1e-3) / 1e9
+    lin_ms, lin_bytes = time_linear_family(km, 1)
+    lm_ms, lm_bytes = time_lm_head(km, 1)
 
     # max over ranks
     t = torch.tensor([ms, e2e_ms, decode_ms_per_tok], dtype=torch.float64, device=dev)
@@ -270,15 +361,13 @@ def run_ours(args, wl):
     ms, e2e_ms, decode_ms_per_tok = t.tolist()
     wb = km.weight_bytes()
     res = dict(
-        metric="decode tok/s/GPU (generated tokens / request time incl. 512-token chunked prefill)",
+        metric=REPLICA_METRIC,
         value=ws * NEW / (ms * 1e-3), unit="tok/s", n_gpus=ws, steps=args.steps,
         warmup=max(args.warmup, 3), ms_per_step=ms, higher_is_better=True, scaling="weak",
         vs_baseline=None, dtype="fp32 act / " + wl["quantize"] + " weights", data="synthetic",
-        config={"workload": args.workload, "model": cfg.name, "quantize": wl["quantize"],
-                "global_batch": ws, "prompt_len": P, "prefill_chunk": C, "new_tokens": NEW,
-                "block_size": B, "parallelism": f"replicas x{ws}",
-                "l2": "inputs larger than L2 (weights streamed per token: "
-                      f"{(wb['layers'] + wb['lm_head']) / 1e6:.0f} MB)"},
+        config=replica_config(wl_name, cfg, wl),
+        parallelism=f"replicas x{ws} (no data-path collective)",
+        per_gpu={"value": NEW / (ms * 1e-3), "unit": "tok/s/GPU"},
         decode_only={"value": ws * 1e3 / decode_ms_per_tok, "unit": "tok/s",
                      "ms_per_token": decode_ms_per_tok,
                      "bytes_per_token": wb["layers"] + wb["lm_head"],
@@ -286,21 +375,36 @@ def run_ours(args, wl):
                      (decode_ms_per_tok * 1e-3) / 1e9 / hbm},
         e2e={"value": ws * NEW / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
              "d2h_bytes_per_step": d2h},
-        roofline={"kernel": "lm_head fp32 GEMV + argmax (ksh_lm_head_argmax)", "bound": "hbm",
-                  "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
-                  "peak_kind": peak_kind,
-                  "traffic": profiled_traffic(f"lm_head_{wl['preset']}"),
-                  "traffic_source": f"profiles/lm_head_{wl['preset']}.md (ncu, one launch)",
-                  "algorithmic_bytes_per_launch": lm_bytes, "launch_ms": lm_ms},
-        gpu_launches=None,
+        roofline=roofline_entry("decode quantized linears of one token (q/k/v, o, gate/up + "
+                                "SwiGLU, down; all layers, one CUDA-graph replay)",
+                                lin_bytes, lin_ms, hbm, peak_kind),
+        roofline_lm_head=roofline_entry("lm_head fp32 GEMV + argmax (ksh_lm_head_argmax)",
+                                        lm_bytes, lm_ms, hbm, peak_kind,
+                                        profiled_traffic(f"lm_head_{wl['preset']}"),
+                                        f"profiles/lm_head_{wl['preset']}.md (ncu, one launch)"),
+        gpu_launches=args.steps * (per_prefill + (NEW - 1) * per_tok),
         clocks=clk.summary(),
     )
-    # this library's kernels per request: prefill + start, then NEW - 1 graph
-    # replays of the decode step
-    res["gpu_launches"] = args.steps * (per_prefill + (NEW - 1) * per_tok)
-    if rank == 0 and not args.no_cpu_baseline and ws == 1:
+    if rank == 0 and with_cpu_baseline and ws == 1:
         res["cpu_baseline"] = cpu_baseline(wl, cfg, prompt, samples=1)
+    st.graph = None
+    del st, km, alloc
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_ours(args, wl):
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
     if ws > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=dev)
+    res = measure_replica(args, wl, args.workload, ws, rank, local, dev,
+                          not args.no_cpu_baseline)
+    if ws > 1:
+        torch.distributed.barrier()
         torch.distributed.destroy_process_group()
     return res, rank
 
@@ -343,10 +447,72 @@ def cpu_baseline(wl, cfg, prompt, samples=1):
     t_dec = statistics.mean(td)
     value = NEW / (t_pref + NEW * t_dec)
     return {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"oracle.model on {threads} threads: {samples}x full {P}-token prefill "
-                      f"({t_pref:.2f}s) + 2 decode tokens ({t_dec:.2f}s/token), "
-                      f"extrapolated to {NEW} tokens",
-            "prefill_s": t_pref, "decode_s_per_token": t_dec}
+            "sample": f"oracle.model on {threads} threads: {samples}x (full {P}-token prefill "
+                      f"({t_pref:.2f}s) + 2 decode tokens ({t_dec:.2f}s/token)); the "
+                      f"{NEW}-token request = prefill + {NEW} decode tokens",
+            "prefill_s": t_pref, "decode_s_per_token": t_dec,
+            "sample_s": t_pref + 2 * t_dec}
+
+
+def cpu_decode_8b(wl, steps, warmup):
+    """The CPU oracle (the reference's algorithm) on config 4's decode step,
+    sampled: the reference serves one request at a time (model.py:103), so a
+    batch of 64 costs 64 single-request decode tokens.  One sample step is one
+    decode token of one request at context ``wl['context']`` through the
+    model cut to ONE layer (INT4/INT8 dequant + linears, RoPE, K/V write,
+    chunked attention over the context, MLP) and through the model with NO
+    layer (embedding, final norm, the untied fp32 lm_head); the full model's
+    token costs ``t0 + 32 * (t1 - t0)``.  K/V of the context are synthetic
+    (the cost does not depend on them).  Returns the sample and per-step
+    times."""
+    import copy
+    from oracle.model import OracleModel
+    from kshipra_b200.config import PRESETS, truncated
+    from kshipra_b200.weights import synthetic_state_dict
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    full = PRESETS[wl["preset"]]
+    cfg1 = truncated(full, 1)
+    sd = synthetic_state_dict(cfg1, seed=0)
+    om1 = OracleModel(cfg1, sd, wl["quantize"])
+    del sd
+    om0 = copy.copy(om1)
+    om0.layers, om0.n_layers = [], 0
+    ctx, bs = wl["context"], wl["block"]
+    nb = ctx // bs + 1
+    pool1 = om1.new_pool(nb, bs).uniform_(-1.0, 1.0)
+    pool0 = om0.new_pool(nb, bs)
+    bt = list(range(nb))
+
+    def token(om, pool):
+        p = ctx
+        om.forward(torch.tensor([[1]]), torch.tensor([[p]]), pool, bt,
+                   [bt[p // bs] * bs + p % bs], prefix_len=p)
+
+    for _ in range(warmup):
+        token(om1, pool1)
+        token(om0, pool0)
+    t1, t0, step_s = [], [], []
+    for _ in range(steps):
+        a = time.perf_counter()
+        token(om1, pool1)
+        b = time.perf_counter()
+        token(om0, pool0)
+        c = time.perf_counter()
+        t1.append(b - a)
+        t0.append(c - b)
+        step_s.append(c - a)
+    m1, m0 = statistics.median(t1), statistics.median(t0)
+    t_tok = m0 + full.layers * max(m1 - m0, 0.0)
+    value = 1.0 / t_tok
+    return {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"oracle.model on {threads} threads, one request at a time: decode token at "
+                      f"context {ctx} through the 1-layer cut ({m1:.2f}s) and the 0-layer cut "
+                      f"({m0:.3f}s), x{steps} steps; {full.layers}-layer token = "
+                      f"t0 + {full.layers}*(t1 - t0) = {t_tok:.2f}s; a batch of "
+                      f"{wl['batch']} costs {wl['batch']} such tokens",
+            "s_per_token_full_model": t_tok, "s_per_layer": m1 - m0, "s_embed_lm_head": m0}, \
+        statistics.mean(step_s)
 
 
 def run_reference(args, wl):
@@ -354,9 +520,19 @@ def run_reference(args, wl):
     if rank != 0:
         return None, rank
     if wl.get("tp"):
-        return {"impl": "reference", "unavailable": "the CPU port is timed on the qwen05b "
-                "workloads; an 8B batch-64 decode at context 4096 does not finish on the host "
-                "cores in minutes"}, rank
+        from kshipra_b200.config import PRESETS
+        cfg = PRESETS[wl["preset"]]
+        cb, step_s = cpu_decode_8b(wl, steps=args.steps, warmup=min(args.warmup, 2))
+        res = dict(metric=TP_METRIC, value=cb["value"], unit="tok/s", n_gpus=ws, steps=args.steps,
+                   warmup=min(args.warmup, 2), ms_per_step=step_s * 1e3, higher_is_better=True,
+                   scaling="strong", vs_baseline=None,
+                   dtype="fp32 act / " + wl["quantize"] + " weights", data="synthetic",
+                   config=tp_config(args.workload, cfg, wl),
+                   parallelism="cpu, one request at a time (the reference's forward is batch 1)",
+                   impl="reference", cpu_baseline=cb,
+                   e2e={"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0})
+        return res, rank
     from kshipra_b200.config import PRESETS
     cfg = PRESETS[wl["preset"]]
     g = torch.Generator().manual_seed(0)
@@ -388,16 +564,16 @@ def run_reference(args, wl):
                         "d2h_bytes_per_step": 0})
         return res, rank
     prompt = torch.randint(0, cfg.vocab, (wl["prompt"],), generator=g).tolist()
-    cb = cpu_baseline(wl, cfg, prompt, samples=max(1, min(args.steps, 2)))
-    res = dict(metric="decode tok/s/GPU (generated tokens / request time incl. 512-token chunked prefill)",
+    # one step = one sample of the request: the full chunked prefill and two
+    # decode tokens (timed), from which the 50-token request rate follows
+    cb = cpu_baseline(wl, cfg, prompt, samples=max(1, args.steps))
+    res = dict(metric=REPLICA_METRIC,
                value=cb["value"], unit="tok/s", n_gpus=ws, steps=args.steps,
-               warmup=args.warmup, ms_per_step=1e3 * wl["new"] / cb["value"],
+               warmup=0, ms_per_step=1e3 * cb["sample_s"],
                higher_is_better=True, scaling="weak", vs_baseline=None,
                dtype="fp32 act / " + wl["quantize"] + " weights", data="synthetic",
-               config={"workload": args.workload, "model": cfg.name, "quantize": wl["quantize"],
-                       "global_batch": 1, "prompt_len": wl["prompt"],
-                       "prefill_chunk": wl["chunk"], "new_tokens": wl["new"],
-                       "block_size": wl["block"], "parallelism": "cpu"},
+               config=replica_config(args.workload, cfg, wl),
+               parallelism="cpu, one request at a time",
                impl="reference", cpu_baseline=cb,
                e2e={"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0})
@@ -585,13 +761,13 @@ def run_tp(args, wl):
     barrier()
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a0.record(stream)
-    for _ in range(min(args.steps, 4)):
+    for _ in range(args.steps):
         st.ids.copy_(h_in, non_blocking=True)
         step()
         h_out.copy_(st.next, non_blocking=True)
     a1.record(stream)
     barrier()
-    e2e_ms = a0.elapsed_time(a1) / min(args.steps, 4)
+    e2e_ms = a0.elapsed_time(a1) / args.steps
 
     # dominant kernel: decode attention of one layer, timed alone
     nb_, L_, _, hkv, bs_, d = pool.shape
@@ -630,42 +806,65 @@ def run_tp(args, wl):
     barrier()
     pf_ms = p0.elapsed_time(p1)
 
-    t = torch.tensor([ms, e2e_ms, attn_ms, pf_ms], dtype=torch.float64, device=dev)
+    # the batch's quantized linears (one graph replay over all layers) and the
+    # vocabulary-parallel lm_head, each timed alone at the step's 64 rows
+    lin_ms, lin_bytes = time_linear_family(km, Bt)
+    lm_ms, lm_bytes = time_lm_head(km, Bt)
+
+    t = torch.tensor([ms, e2e_ms, attn_ms, pf_ms, lin_ms, lm_ms], dtype=torch.float64, device=dev)
     if ws > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    ms, e2e_ms, attn_ms, pf_ms = t.tolist()
+    ms, e2e_ms, attn_ms, pf_ms, lin_ms, lm_ms = t.tolist()
     hbm, _, peak_kind = measured_peaks()
     wb = km.weight_bytes()
     step_bytes = wb["layers"] + wb["lm_head"] + L_ * attn_bytes
-    achieved = attn_bytes / (attn_ms * 1e-3) / 1e9
     res = dict(
-        metric="decode tok/s/GPU (generated tokens / decode step time, batch 64 at context 4096)",
+        metric=TP_METRIC,
         value=Bt / (ms * 1e-3), unit="tok/s", n_gpus=ws, steps=args.steps,
         warmup=max(args.warmup, 3), ms_per_step=ms, higher_is_better=True, scaling="strong",
         vs_baseline=None, dtype="fp32 act / " + wl["quantize"] + " weights", data="synthetic",
-        config={"workload": args.workload, "model": cfg.name, "quantize": wl["quantize"],
-                "global_batch": Bt, "context": ctx, "block_size": bs,
-                "parallelism": f"tp{ws}", "kv_cache": "synthetic values (fp32)",
-                "decode_graph": graph,
-                "l2": f"inputs larger than L2 ({step_bytes / 1e9:.1f} GB read per step on rank 0)"},
+        config=tp_config(args.workload, cfg, wl),
+        parallelism=(f"tensor parallel x{ws}: heads, MLP rows and vocabulary split, two NCCL "
+                     "all-reduces per layer" if ws > 1 else "one GPU (tp1)"),
+        decode_graph=graph,
         per_gpu={"value": Bt / (ms * 1e-3) / ws, "unit": "tok/s/GPU"},
         decode_step={"bytes_rank0": step_bytes,
-                     "hbm_frac_of_" + peak_kind: step_bytes / (ms * 1e-3) / 1e9 / hbm},
+                     "hbm_frac_of_" + peak_kind: step_bytes / (ms * 1e-3) / 1e9 / hbm,
+                     "share_attention": L_ * attn_ms / ms, "share_linears": lin_ms / ms,
+                     "share_lm_head": lm_ms / ms},
         prefill={"tokens": PF, "ms": pf_ms, "tok_s": PF / (pf_ms * 1e-3)},
         e2e={"value": Bt / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": Bt * 8,
              "d2h_bytes_per_step": Bt * 8},
-        roofline={"kernel": "fused decode attention (ksh_decode_attention), one layer",
-                  "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                  "frac": achieved / hbm, "peak_kind": peak_kind,
-                  "traffic": profiled_traffic("decode_attention_llama8b_b64_ctx4096") if ws == 1 else None,
-                  "traffic_source": "profiles/decode_attention_llama8b_b64_ctx4096.md (ncu, one launch, TP1)",
-                  "algorithmic_bytes_per_launch": attn_bytes, "launch_ms": attn_ms},
+        roofline=roofline_entry(
+            "fused decode attention (ksh_decode_attention), one layer",
+            attn_bytes, attn_ms, hbm, peak_kind,
+            profiled_traffic("decode_attention_llama8b_b64_ctx4096") if ws == 1 else None,
+            "profiles/decode_attention_llama8b_b64_ctx4096.md (ncu, one launch, TP1)"),
+        roofline_linears=roofline_entry(
+            "batched-decode quantized linears of one step at 64 rows (q/k/v, o, gate/up + "
+            "SwiGLU, down; all layers, one CUDA-graph replay)", lin_bytes, lin_ms, hbm, peak_kind),
+        roofline_lm_head=roofline_entry(
+            "batch lm_head + argmax at 64 rows (ksh_lm_head_argmax, vocabulary shard)",
+            lm_bytes, lm_ms, hbm, peak_kind),
         gpu_launches=args.steps * per_step,
         clocks=clk.summary(),
     )
     if graph:
         st.graph = None                 # release the captured NCCL calls before teardown
     torch.cuda.synchronize()
+    del st, km, pool, alloc
+    torch.cuda.empty_cache()
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"], _ = cpu_decode_8b(wl, steps=2, warmup=1)
+    if not args.no_replica:
+        # the 0.5B batch-1 request workload (config 2) beside it: one
+        # independent replica per rank
+        rep = measure_replica(args, WORKLOADS["qwen05b-int8"], "qwen05b-int8", ws, rank, local,
+                              dev, with_cpu_baseline=False)
+        res["qwen05b_int8"] = {k: rep[k] for k in ("metric", "value", "unit", "ms_per_step",
+                                                   "config", "parallelism", "per_gpu",
+                                                   "decode_only", "e2e", "roofline",
+                                                   "roofline_lm_head", "gpu_launches")}
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -1123,8 +1322,10 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="qwen05b-int8", choices=sorted(WORKLOADS) + ["micro"])
+    ap.add_argument("--workload", default="llama8b-int4", choices=sorted(WORKLOADS) + ["micro"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-replica", action="store_true",
+                    help="default workload: skip the 0.5B replica figures reported beside it")
     ap.add_argument("--profile", action="store_true",
                     help="run one request inside cudaProfilerStart/Stop (for ncu)")
     ap.add_argument("--trace", action="store_true",

@@ -10,6 +10,11 @@
  * position, token id, non-finite weight) are OR-ed into a caller-owned int32
  * status word as KSH_FLAG_* bits; kernels never trap.
  *
+ * Workspaces need no initialisation: the entry points that keep completion
+ * counters in a workspace (ksh_paged_attention, ksh_lm_head_argmax) clear
+ * them on the caller's stream before their kernels run, so a buffer fresh
+ * from cudaMalloc (or torch.empty) is a valid workspace.
+ *
  * Functions are stateless and may be called from any host thread; calls on
  * one stream are ordered, calls on different streams that share a workspace
  * race.
@@ -249,6 +254,20 @@ int ksh_decode_advance(const int64_t* next, int64_t batch, int64_t* ids,
                        const int32_t* block_tables, int64_t max_blocks,
                        int64_t block_size, int64_t* history, int64_t hist_stride,
                        int64_t* step, int32_t* flags, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Failure-path check of the device waits (no counterpart in the reference;
+ * it stands in for the reference's timeout-and-report handling of a stuck
+ * worker, benchmarks/run_benchmarks.py:234-267, at the device level).  One
+ * CTA waits, with the same bounded primitives the pipelined kernels use, on
+ * an mbarrier phase and on the device word *wait_flag; unless `arrive` is
+ * set nothing completes either, so each wait gives up after `polls` attempts
+ * (1 .. 2^24), KSH_FLAG_TIMEOUT is OR-ed into *flags and *where (optional)
+ * gets bit 0 for the mbarrier, bit 1 for the flag.  The kernel then returns,
+ * leaving the context usable.
+ * ---------------------------------------------------------------------- */
+int ksh_check_bounded_wait(int64_t polls, int arrive, const int32_t* wait_flag,
+                           int32_t* flags, int32_t* where, void* stream);
 
 #ifdef __cplusplus
 }

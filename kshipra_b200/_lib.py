@@ -59,6 +59,7 @@ SIGNATURES = {
     "ksh_lm_head_argmax_noalloc": (I32, [P, I64, I64, P, F32, P, I64, P, P, P]),
     "ksh_argmax_rows": (I32, [P, I64, I64, P, P]),
     "ksh_decode_advance": (I32, [P, I64, P, P, P, P, P, I64, I64, P, I64, P, P, P]),
+    "ksh_check_bounded_wait": (I32, [I64, I32, P, P, P, P]),
 }
 
 

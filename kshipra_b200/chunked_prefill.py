@@ -122,8 +122,12 @@ class ChunkedPrefillEngine:
         self.head_dim = head_dim
         self.gqa_ratio = num_heads // num_kv_heads
 
-    def prefill(self, token_ids: List[int], embedding_layer, rope_fn, layer_fn,
-                use_oracle: bool = False) -> torch.Tensor:
+    def prefill(self, token_ids: List[int], embedding_layer, rope_fn, layer_fn) -> torch.Tensor:
+        """Chunked prefill of ``token_ids`` after the prefix the radix tree
+        holds (chunked_prefill.py:168-246).  Each chunk's rotated K and V are
+        written into its blocks of the pool in one indexed store per chunk
+        (every layer of the pool, as the reference's scatter does), then the
+        chunk attends over the pool's layer-0 views on the GPU."""
         P = len(token_ids)
         matched_blocks, matched_len, node = self.cache.tree.match(token_ids)
         self.cache.tree.pin(node)
@@ -132,6 +136,7 @@ class ChunkedPrefillEngine:
         new_blocks = self.cache.allocate_blocks(need)
         block_table = matched_blocks + new_blocks
         pool = self.cache.allocator.pool
+        bt_dev = torch.as_tensor(block_table, dtype=torch.int64, device=pool.device)
         pos = matched_len
         hidden = None
         while pos < P:
@@ -142,12 +147,12 @@ class ChunkedPrefillEngine:
             def attn_fn(q, k, v, pos=pos, C=C):
                 positions = pos + torch.arange(C, device=q.device)
                 q, k = rope_fn(q, k, positions)
-                blk_idx, offset = pos // self.block_size, pos % self.block_size
-                for i in range(C):
-                    b_id = block_table[blk_idx + (offset + i) // self.block_size]
-                    o = (offset + i) % self.block_size
-                    pool[b_id, :, 0, :, o, :] = k[:, i, :]
-                    pool[b_id, :, 1, :, o, :] = v[:, i, :]
+                p = torch.arange(pos, pos + C, device=pool.device)
+                blk = bt_dev[p // self.block_size]
+                off = p % self.block_size
+                # pool[blk[i], :, 0 | 1, :, off[i], :] = k | v[:, i, :] for all i
+                pool[blk, :, 0, :, off, :] = k.transpose(0, 1).unsqueeze(1).to(pool.dtype)
+                pool[blk, :, 1, :, off, :] = v.transpose(0, 1).unsqueeze(1).to(pool.dtype)
                 return chunked_attention(q, pool[:, 0, 0], pool[:, 0, 1], block_table,
                                          prefix_len=pos, chunk_len=C, block_size=self.block_size)
 

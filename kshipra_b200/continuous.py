@@ -9,7 +9,9 @@ Interface and scheduling policy follow the reference's engine/continuous.py:
 * per iteration, every RUNNING request decodes one token and the prefill
   token budget ``int(itl_budget / t_tok) - n_decodes`` is handed out in
   chunks to PREFILLING requests in admission order (:148-183);
-* swap-out preemption of a victim's blocks to host memory (:206-223).
+* swap-out preemption of a victim's blocks to pinned host memory
+  (:206-223), asynchronous on a side stream, and swap-in that resumes the
+  request where it stopped.
 
 Without a model the step sleeps ``total_tokens * t_tok_s`` like the
 reference's simulated forward (:229-261), so the scheduling decisions are
@@ -72,6 +74,20 @@ class SchedulerOutput:
     decodes: List[Request]
     prefills: List[Tuple[Request, int]]
     total_tokens: int
+
+
+def _runs(blocks: List[int], start: int = 0):
+    """(index, first block, count) for each run of consecutive block ids, so a
+    swap copies whole contiguous ranges of the pool at once."""
+    out = []
+    i = 0
+    while i < len(blocks):
+        j = i + 1
+        while j < len(blocks) and blocks[j] == blocks[j - 1] + 1:
+            j += 1
+        out.append((start + i, blocks[i], j - i))
+        i = j
+    return out
 
 
 class ContinuousEngine:
@@ -154,8 +170,7 @@ class ContinuousEngine:
         req.block_table = matched + new
         req.state = SeqState.PREFILLING
         if req.swapped_kv is not None:
-            req.prefill_pos = len(req.prompt_tokens)
-            self._swap_in(req)
+            self._swap_in(req, len(matched))
         elif self.model is not None:
             req.prefill_pos = matched_len             # the tree's blocks hold these positions
 
@@ -184,15 +199,41 @@ class ContinuousEngine:
     # ---------------- preemption ----------------
 
     def _preempt(self, victim: Request) -> None:
+        """Swap the victim's K/V blocks out to pinned host memory and requeue
+        it at the head of the waiting queue (continuous.py:206-223).
+
+        On a CUDA pool the device-to-host copies run on a side stream, after
+        the work already queued on the current stream (so they see the
+        victim's latest K/V); the current stream then waits on the copies'
+        event, a device-side wait, so no later kernel can overwrite the freed
+        blocks before they are saved and the host never blocks.  The event is
+        kept on the request (``swap_event``) for a caller that wants to read
+        ``swapped_kv`` on the host.  The request resumes where it stopped:
+        a decoding request comes back RUNNING, a partly prefilled one
+        PREFILLING at the same prompt position (the reference comes back
+        PREFILLING at the prompt's end, where its scheduler never picks the
+        request up again)."""
+        victim._resume_running = victim.state == SeqState.RUNNING  # type: ignore[attr-defined]
+        victim._resume_pos = victim.prefill_pos  # type: ignore[attr-defined]
         victim.state = SeqState.WAITING
         if victim.block_table:
             pool = self.cache.allocator.pool
-            idx = torch.tensor(victim.block_table, dtype=torch.long, device=pool.device)
-            host = torch.empty((len(victim.block_table), *pool.shape[1:]), dtype=pool.dtype,
-                               pin_memory=pool.is_cuda)
-            host.copy_(pool.index_select(0, idx), non_blocking=pool.is_cuda)
+            n = len(victim.block_table)
+            host = torch.empty((n, *pool.shape[1:]), dtype=pool.dtype, pin_memory=pool.is_cuda)
             if pool.is_cuda:
-                torch.cuda.current_stream(pool.device).synchronize()
+                cur = torch.cuda.current_stream(pool.device)
+                side = self._side_stream(pool.device)
+                side.wait_stream(cur)
+                with torch.cuda.stream(side):
+                    for i0, b0, cnt in _runs(victim.block_table):
+                        host[i0:i0 + cnt].copy_(pool[b0:b0 + cnt], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(side)
+                cur.wait_event(ev)
+                victim.swap_event = ev  # type: ignore[attr-defined]
+            else:
+                for i0, b0, cnt in _runs(victim.block_table):
+                    host[i0:i0 + cnt].copy_(pool[b0:b0 + cnt])
             # blocks the request took from (or gave to) the radix tree stay the tree's
             for b in getattr(victim, "_own_blocks", victim.block_table):
                 self.cache.allocator.free(b)
@@ -203,12 +244,33 @@ class ContinuousEngine:
         self.waiting_queue.insert(0, victim)
         self.active_sequences.pop(victim.req_id, None)
 
-    def _swap_in(self, req: Request) -> None:
+    def _side_stream(self, device) -> "torch.cuda.Stream":
+        s = getattr(self, "_swap_stream", None)
+        if s is None:
+            s = torch.cuda.Stream(device=device)
+            self._swap_stream = s
+        return s
+
+    def _swap_in(self, req: Request, n_matched: int) -> None:
+        """Copy the swapped K/V back into the request's own blocks.  The first
+        ``n_matched`` entries of its new block table come from the radix tree
+        (the same tokens' K/V, possibly pinned and read by other requests), so
+        they are left as they are."""
         pool = self.cache.allocator.pool
         n = min(len(req.block_table), req.swapped_kv.shape[0])
-        idx = torch.tensor(req.block_table[:n], dtype=torch.long, device=pool.device)
-        pool.index_copy_(0, idx, req.swapped_kv[:n].to(pool.device, non_blocking=True))
+        if pool.is_cuda:
+            ev = getattr(req, "swap_event", None)
+            if ev is not None:
+                torch.cuda.current_stream(pool.device).wait_event(ev)
+        for i0, b0, cnt in _runs(req.block_table[n_matched:n], start=n_matched):
+            pool[b0:b0 + cnt].copy_(req.swapped_kv[i0:i0 + cnt], non_blocking=pool.is_cuda)
         req.swapped_kv = None
+        req.swap_event = None  # type: ignore[attr-defined]
+        if getattr(req, "_resume_running", True):
+            req.prefill_pos = len(req.prompt_tokens)
+            req.state = SeqState.RUNNING
+        else:
+            req.prefill_pos = getattr(req, "_resume_pos", 0)
 
     # ---------------- step ----------------
 

@@ -477,6 +477,13 @@ extern "C" int ksh_paged_attention(const float* q, int64_t hq, int64_t d, const 
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return KSH_ERR_ALIGN;
   a.counters = static_cast<uint32_t*>(workspace);
   a.part = reinterpret_cast<float*>(static_cast<char*>(workspace) + p.counter_bytes);
+  if (p.nsplit > 1) {
+    // The split counters must start at zero.  The last CTA of each item
+    // resets its counter, but the caller's workspace may hold anything on
+    // its first use, so clear them here on the caller's stream.
+    const cudaError_t e = cudaMemsetAsync(workspace, 0, static_cast<size_t>(p.items) * 4, st);
+    if (e != cudaSuccess) return record_cuda_error(e);
+  }
   a.qt = p.qt;
   a.nqt = p.nqt;
   a.nsplit = p.nsplit;

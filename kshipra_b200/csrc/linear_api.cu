@@ -248,6 +248,10 @@ extern "C" int ksh_lm_head_argmax(const float* x, int64_t m, int64_t hidden,
     char* ws = static_cast<char*>(workspace);
     const int64_t grid = gemv_argmax_grid(vocab);
     a.counter = reinterpret_cast<uint32_t*>(ws);
+    // The completion counter must start at zero whatever the workspace held.
+    const cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(uint32_t),
+                                          static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return record_cuda_error(e);
     a.part_val = reinterpret_cast<float*>(ws + kLmHeadHeader);
     a.part_idx = reinterpret_cast<int32_t*>(ws + kLmHeadHeader + grid * m * 4);
     a.argmax_out = tokens;

@@ -328,6 +328,10 @@ int launch_lm_gemm(const float* x, int64_t m, int64_t k, const float* norm_w, fl
                           CU_TENSOR_MAP_SWIZZLE_128B))
     return KSH_ERR_UNSUPPORTED;
   float* inv = reinterpret_cast<float*>(ws + 256);
+  // Completion counter and error word must start at zero whatever the
+  // workspace held; the last CTA leaves both at zero for the next launch.
+  const cudaError_t e = cudaMemsetAsync(ws, 0, 2 * sizeof(uint32_t), stream);
+  if (e != cudaSuccess) return record_cuda_error(e);
   if (norm_w) {
     int st = launch(lm_inv_rms_kernel, dim3(static_cast<unsigned>(m)), dim3(256), 0, stream, x,
                     static_cast<int>(k), eps, inv);

@@ -141,7 +141,47 @@ int resident_ctas(const void* kernel, int threads, size_t smem) {
   return n;
 }
 
+namespace {
+// The library's two forms of device wait, run on something nothing will ever
+// complete unless `arrive` is set: an mbarrier phase (as the TMA / tcgen05
+// pipelines wait) and a flag word in global memory (as an inter-CTA or
+// inter-GPU hand-off waits).  Each gives up after `polls` attempts with the
+// same primitive the kernels use and raises KSH_FLAG_TIMEOUT; `where`
+// records which wait gave up (1 = mbarrier, 2 = flag) for the host.
+__global__ void bounded_wait_check_kernel(uint32_t polls, int arrive,
+                                          const volatile int32_t* gflag, int32_t* flags,
+                                          int32_t* where) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&bar, 1);
+    tc::fence_barrier_init();
+  }
+  __syncthreads();
+  if (arrive && threadIdx.x == 0) tc::mbar_arrive(&bar);
+  const bool ok_bar = tc::mbar_wait(&bar, 0, polls);
+  bool ok_flag = arrive != 0;
+  if (!arrive) {
+    for (uint32_t i = 0; i < polls && !ok_flag; ++i) {
+      ok_flag = *gflag != 0;
+      if (!ok_flag) __nanosleep(32);
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (!ok_bar || !ok_flag) raise_flag(flags, KSH_FLAG_TIMEOUT);
+    if (where) *where = (ok_bar ? 0 : 1) | (ok_flag ? 0 : 2);
+  }
+}
+}  // namespace
+
 }  // namespace ksh
+
+extern "C" int ksh_check_bounded_wait(int64_t polls, int arrive, const int32_t* wait_flag,
+                                      int32_t* flags, int32_t* where, void* stream) {
+  KSH_CHECK_ARG(polls > 0 && polls <= (1LL << 24) && wait_flag && flags);
+  return ksh::launch(ksh::bounded_wait_check_kernel, dim3(1), dim3(32), 0,
+                     static_cast<cudaStream_t>(stream), static_cast<uint32_t>(polls), arrive,
+                     wait_flag, flags, where);
+}
 
 extern "C" int ksh_abi_version(void) { return 1; }
 

@@ -45,7 +45,8 @@ from .quantization import (QuantizedLinear, QuantizedWeight, Workspace, linear_l
 
 FLAG_NAMES = {1: "non-finite weight", 2: "block id out of range", 4: "slot out of range",
               8: "position outside the RoPE table", 16: "token id out of range",
-              32: "sequence longer than its block table"}
+              32: "sequence longer than its block table", 64: "a bounded device wait gave up"}
+FLAG_TIMEOUT = 64
 
 
 # GQA group sizes the fused decode-attention kernel is instantiated for, per head dim.
@@ -56,12 +57,19 @@ class KshipraDeviceError(IndexError):
     """A kernel reported a data-dependent error through the device status word."""
 
 
+class KshipraDeviceTimeout(TimeoutError):
+    """A kernel's bounded wait gave up (KSH_FLAG_TIMEOUT); its outputs are invalid."""
+
+
 def _check_flags(flags: torch.Tensor) -> None:
     f = int(flags.item())
     if f:
         names = [n for b, n in FLAG_NAMES.items() if f & b]
         flags.zero_()
-        raise KshipraDeviceError("device reported: " + ", ".join(names))
+        msg = "device reported: " + ", ".join(names)
+        if f & FLAG_TIMEOUT:
+            raise KshipraDeviceTimeout(msg)
+        raise KshipraDeviceError(msg)
 
 
 def rope_tables(head_dim: int, theta: float, max_pos: int):

@@ -134,3 +134,50 @@ def mask_kat_inputs():
 def prompt_ids(vocab: int, n: int, seed: int = 0) -> List[int]:
     g = torch.Generator().manual_seed(seed)
     return torch.randint(0, vocab, (n,), generator=g).tolist()
+
+
+def batch_prompts(vocab: int, n: int, lo: int, hi: int, seed: int) -> List[List[int]]:
+    """``n`` prompts of uniform random ids, lengths uniform in [lo, hi]."""
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(lo, hi + 1, (n,), generator=g).tolist()
+    return [torch.randint(0, vocab, (ln,), generator=g).tolist() for ln in lens]
+
+
+# Llama-3-8B shape cut to two layers (head_dim 128, 32 / 8 heads, untied
+# lm_head, vocabulary 128256): one request chunk-prefilled in 16-token chunks
+# with per-step logits, and a batch of short requests (4 greedy tokens each).
+L8B_PROMPT, L8B_CHUNK, L8B_NEW = 64, 16, 12
+L8B_BATCH, L8B_BATCH_NEW = 20, 4
+
+
+def llama8b_l2():
+    from kshipra_b200.config import LLAMA3_8B, truncated
+    return truncated(LLAMA3_8B, 2)
+
+
+def llama8b_batch_prompts(vocab: int) -> List[List[int]]:
+    return batch_prompts(vocab, L8B_BATCH, 5, 40, seed=31)
+
+
+# Config-3 requests, shortened: the first 40 draws of the config's Poisson
+# trace (benchmarks/traffic.py:23-55 semantics: 8 req/s, prompts 256-2048,
+# seed 42; the first 32 are the benchmark's own trace), each prompt length
+# divided by 32, behind one of two 32-token system prefixes (request i uses
+# prefix i % 2) so that a second wave of requests finds the first wave's
+# prompt blocks in the radix tree.  Qwen2.5-0.5B shape, INT4, 5 greedy tokens.
+CB_REQUESTS, CB_WAVE, CB_NEW, CB_SYSTEM = 40, 20, 5, 32
+
+
+def cb_requests(vocab: int) -> List[List[int]]:
+    import importlib.util
+    import os
+    root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    spec = importlib.util.spec_from_file_location("_bench_trace", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    trace = bench.poisson_trace(CB_REQUESTS, 8.0, (256, 2048), (128, 128), 42)
+    systems = [prompt_ids(vocab, CB_SYSTEM, seed=100 + s) for s in range(2)]
+    out = []
+    for i, (_, plen, _) in enumerate(trace):
+        out.append(systems[i % 2] + prompt_ids(vocab, plen // 32, seed=200 + i))
+    return out

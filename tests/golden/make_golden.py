@@ -19,6 +19,15 @@ stored (inputs are regenerated from their seeds by the tests):
                           tokens and per-step logits for int8 / int4 / fp32
 * ``model_qwen05b.npz`` -- the same on the Qwen2.5-0.5B shape (int8, int4):
                           tokens, top-2 margins, logits after the prefill
+* ``model_llama8b_l2.npz`` -- the Llama-3-8B shape cut to two layers (int8,
+                          int4): one 64-token prompt in 16-token chunks + 12
+                          greedy tokens (tokens, margins, logits of the first
+                          and last step), and 20 short prompts with 4 greedy
+                          tokens each (tokens, margins)
+* ``model_cb_requests.npz`` -- 40 shortened config-3 requests (two 32-token
+                          system prefixes + Poisson-trace suffixes) on the
+                          Qwen2.5-0.5B shape, int4, 5 greedy tokens each,
+                          every request run alone (tokens, margins)
 * ``cache_trace.json`` -- block allocator / radix tree / scheduler decisions on
                           a deterministic operation sequence (prefix_cache.py,
                           continuous.py), with the clock replaced by a counter.
@@ -162,6 +171,50 @@ def make_model_05b(out_dir):
     np.savez_compressed(os.path.join(out_dir, "model_qwen05b.npz"), **d)
 
 
+def _margins(logs):
+    top = torch.topk(torch.stack(logs), 2, dim=-1).values
+    return (top[:, 0] - top[:, 1]).numpy()
+
+
+def make_model_8b(out_dir):
+    cfg = cases.llama8b_l2()
+    sd = synthetic_state_dict(cfg, seed=0)
+    prompt = cases.prompt_ids(cfg.vocab, cases.L8B_PROMPT, seed=0)
+    batch = cases.llama8b_batch_prompts(cfg.vocab)
+    d = {"prompt": np.array(prompt), "weights_checksum": np.array(weights_checksum(sd))}
+    for q in ("int8", "int4"):
+        t0 = time.time()
+        km = _kshipra(cfg, sd, q)
+        toks, logs = _ref_generate(km, prompt, cases.L8B_NEW, block_size=16,
+                                   chunk=cases.L8B_CHUNK)
+        d[f"{q}/tokens"] = np.array(toks)
+        d[f"{q}/margins"] = _margins(logs)
+        d[f"{q}/logits_first"] = logs[0].numpy()
+        d[f"{q}/logits_last"] = logs[-1].numpy()
+        for i, p in enumerate(batch):
+            bt, bl = _ref_generate(km, p, cases.L8B_BATCH_NEW, block_size=16, chunk=len(p))
+            d[f"{q}/batch{i}/tokens"] = np.array(bt)
+            d[f"{q}/batch{i}/margins"] = _margins(bl)
+        print(f"  8B-L2 {q}: {time.time() - t0:.1f}s tokens[:8]={toks[:8]}", flush=True)
+        del km
+    np.savez_compressed(os.path.join(out_dir, "model_llama8b_l2.npz"), **d)
+
+
+def make_cb_requests(out_dir):
+    cfg = QWEN25_05B
+    sd = synthetic_state_dict(cfg, seed=0)
+    reqs = cases.cb_requests(cfg.vocab)
+    d = {"weights_checksum": np.array(weights_checksum(sd))}
+    km = _kshipra(cfg, sd, "int4")
+    t0 = time.time()
+    for i, p in enumerate(reqs):
+        toks, logs = _ref_generate(km, p, cases.CB_NEW, block_size=16, chunk=len(p))
+        d[f"req{i}/tokens"] = np.array(toks)
+        d[f"req{i}/margins"] = _margins(logs)
+    print(f"  cb requests: {time.time() - t0:.1f}s", flush=True)
+    np.savez_compressed(os.path.join(out_dir, "model_cb_requests.npz"), **d)
+
+
 class _Clock:
     def __init__(self):
         self.t = 0.0
@@ -273,7 +326,8 @@ def main():
     steps = [("quant", make_quant), ("qlinear", make_qlinear), ("attention", make_attention),
              ("model_tiny", make_model_tiny), ("cache_trace", make_cache_trace)]
     if not a.skip_05b:
-        steps.append(("model_qwen05b", make_model_05b))
+        steps += [("model_qwen05b", make_model_05b), ("model_llama8b_l2", make_model_8b),
+                  ("model_cb_requests", make_cb_requests)]
     for name, fn in steps:
         if a.only and name not in a.only.split(","):
             continue

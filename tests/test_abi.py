@@ -63,3 +63,22 @@ def test_argument_errors_are_reported_without_a_launch():
     assert h.ksh_pack_int4(None, 4, 4, 3, None, None, None, None) == -1
     with pytest.raises(_lib.KshipraLibraryError):
         _lib.call("ksh_rmsnorm", None, None, None, 1, 0, 1e-6, None)
+
+
+def test_bounded_wait_check_rejects_bad_limits_on_the_host():
+    h = _lib.lib()
+    fake = 256          # never dereferenced: the limits are checked before any launch
+    assert h.ksh_check_bounded_wait(0, 0, fake, fake, None, None) == -1
+    assert h.ksh_check_bounded_wait(1 << 25, 0, fake, fake, None, None) == -1
+    assert h.ksh_check_bounded_wait(100, 0, None, fake, None, None) == -1
+
+
+def test_noalloc_scratch_covers_the_largest_argmax_grid():
+    """The fused lm_head GEMV's argmax grid is at most 8 CTAs per SM
+    (gemv.cu, gemv_argmax_grid) and keeps one (max, index) pair of 8 bytes
+    per CTA and row behind a 256-byte header; for the 16 rows the
+    no-allocation entry point accepts, on a 148-SM B200, that must fit its
+    fixed array."""
+    h = _lib.lib()
+    sms, max_rows = 148, 16
+    assert 256 + sms * 8 * max_rows * 8 <= h.ksh_lm_head_argmax_noalloc_max_bytes()

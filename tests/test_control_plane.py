@@ -11,6 +11,7 @@ import os
 import time
 
 import pytest
+import torch
 
 import make_golden
 from kshipra_b200 import continuous as kc
@@ -130,10 +131,37 @@ def test_preemption_swap():
     e.schedule()
     assert len(r.block_table) == 11 and len(e.cache.allocator.free_blocks) == 1
     r.prefill_pos, r.state = 640, SeqState.RUNNING
+    pool = e.cache.allocator.pool
+    pool[r.block_table] = torch.arange(11, dtype=pool.dtype).view(
+        11, 1, 1, 1, 1, 1).expand(11, *pool.shape[1:])
+    r.generated_tokens = [0, 0, 0]
     e._preempt(r)
     assert r.state == SeqState.WAITING and r.block_table == []
     assert r.swapped_kv is not None and r.swapped_kv.shape[0] == 11
     assert len(e.cache.allocator.free_blocks) == 12
+    assert e.waiting_queue[0] is r
+    # re-admission restores the K/V into the new blocks and resumes decoding
+    s = e.schedule()
+    assert r.state == SeqState.RUNNING and s.decodes == [r] and s.prefills == []
+    assert r.swapped_kv is None and len(r.block_table) == 11
+    got = e.cache.allocator.pool[r.block_table][:, 0, 0, 0, 0, 0]
+    assert got.tolist() == [float(i) for i in range(11)]
+    while r.state != SeqState.FINISHED:
+        e.step()
+    assert len(r.generated_tokens) == 10 and r in e.finished
+    assert len(e.cache.allocator.free_blocks) == 12
+
+
+def test_preemption_mid_prefill_resumes_at_its_position():
+    e = _engine(12)
+    r = e.add_request([0] * 100, 10)
+    s = e.schedule()
+    assert s.prefills and s.prefills[0][0] is r
+    r.prefill_pos = 48
+    e._preempt(r)
+    s = e.schedule()
+    assert r.state == SeqState.PREFILLING and r.prefill_pos == 48
+    assert s.prefills == [(r, min(52, s.prefills[0][1]))]
 
 
 def test_itl_budget_bound():

@@ -499,6 +499,64 @@ def test_lm_head_argmax_tiled_x_stays_in_workspace(m, H, V):
         assert int(tok[0]) == V // 3
 
 
+@pytest.mark.parametrize("m", [1, 16, 40])
+def test_lm_head_argmax_accepts_uninitialised_workspace(m):
+    """A workspace straight from the allocator (here filled with 0xFF bytes)
+    is valid: the entry point clears its completion counter before the
+    kernels run, for the GEMV path (<= 16 rows) and the batch path."""
+    from kshipra_b200 import _lib
+    gen = torch.Generator().manual_seed(40 + m)
+    V, H = 50000, 1024
+    w = (torch.randn((V, H), generator=gen) * 0.02).cuda()
+    x = torch.randn((m, H), generator=gen).cuda()
+    need = int(_lib.lib().ksh_lm_head_workspace_size(m, V))
+    out = {}
+    for fill in (0x00, 0xFF):
+        ws = torch.full((need,), fill, dtype=torch.uint8, device="cuda")
+        lg = torch.empty((m, V), device="cuda")
+        tok = torch.full((m,), -1, dtype=torch.int64, device="cuda")
+        for _ in range(2):
+            _lib.call("ksh_lm_head_argmax", x.data_ptr(), m, H, None, 0.0, w.data_ptr(), V,
+                      lg.data_ptr(), tok.data_ptr(), ws.data_ptr(), need, _lib.stream_ptr())
+            torch.cuda.synchronize()
+            out.setdefault(fill, []).append((tok.cpu().tolist(), lg.cpu()))
+    ref = torch.argmax(out[0][0][1], dim=1).tolist()
+    for fill in (0x00, 0xFF):
+        for toks, lg in out[fill]:
+            assert toks == ref, fill
+            assert torch.equal(lg, out[0][0][1])
+
+
+def test_paged_attention_accepts_uninitialised_workspace():
+    """Split-K attention with its counters in a 0xFF-filled workspace gives
+    the result of a zeroed one (the entry point clears the counters)."""
+    from kshipra_b200.chunked_prefill import AttentionWorkspace, paged_attention
+    gen = torch.Generator().manual_seed(3)
+    nb, L, hkv, B, D, hq = 80, 2, 2, 16, 64, 14
+    pool = torch.randn((nb, L, 2, hkv, B, D), generator=gen).cuda()
+    P, C = 700, 3
+    nblk = (P + C + B - 1) // B
+    bt = torch.arange(nblk, dtype=torch.int32).view(1, -1).cuda()
+    q = torch.randn((C, hq, D), generator=gen).cuda()
+    qs = torch.tensor([0, C], dtype=torch.int32).cuda()
+    pl = torch.tensor([P], dtype=torch.int32).cuda()
+    res = []
+    for fill in (0x00, 0xFF):
+        ws = AttentionWorkspace()
+        ws.buf = torch.full((1 << 22,), fill, dtype=torch.uint8, device="cuda")
+        out = torch.empty_like(q)
+        flags = torch.zeros(1, dtype=torch.int32, device="cuda")
+        for _ in range(2):
+            paged_attention(q, pool, 1, bt, qs, pl, C, P + C, out, flags, ws=ws)
+            res.append(out.cpu().clone())
+        assert int(flags.item()) == 0
+    ref = oa.chunked_attention(q.cpu().transpose(0, 1), pool.cpu()[:, 1, 0], pool.cpu()[:, 1, 1],
+                               list(range(nblk)), P, C, B).transpose(0, 1)
+    for r in res:
+        assert torch.equal(r, res[0])
+    assert rel_l2(res[0].numpy(), ref.numpy()) < 1e-5
+
+
 @pytest.mark.parametrize("scheme", ["int8", "int4"])
 @pytest.mark.parametrize("m,k,n", [(128, 896, 1152), (512, 4864, 896), (130, 896, 9728),
                                    (2048, 4096, 512)])
@@ -711,3 +769,68 @@ def test_fused_decode_attention_long_context_batch64():
                 got = out[b, hk * g:(hk + 1) * g].double()
                 err = float((got - ref).norm() / ref.norm())
                 assert err < 1e-5, (split, b, hk, err)
+
+
+def test_chunked_prefill_engine_mock_layer_vs_cpu():
+    """ChunkedPrefillEngine.prefill (chunked_prefill.py:148-246) with a mock
+    one-layer model: each chunk's rotated K / V land in the pool at their
+    slots (every layer of the pool, as the reference writes them), and the
+    last chunk's attention over the whole prompt matches a float64 causal
+    softmax on the CPU."""
+    from kshipra_b200.chunked_prefill import ChunkedPrefillEngine
+    from kshipra_b200.prefix_cache import PrefixCache
+    gen = torch.Generator().manual_seed(21)
+    V, H, HKV, D, B, P, CH = 500, 4, 2, 64, 16, 70, 16
+    emb = torch.randn((V, 128), generator=gen)
+    wq = torch.randn((128, H * D), generator=gen) * 0.1
+    wk = torch.randn((128, HKV * D), generator=gen) * 0.1
+    wv = torch.randn((128, HKV * D), generator=gen) * 0.1
+    ids = torch.randint(0, V, (P,), generator=gen).tolist()
+    cache = PrefixCache(num_blocks=12, block_size=B, num_layers=2, num_kv_heads=HKV, head_dim=D,
+                        dtype=torch.float32, device=torch.device("cuda"))
+    eng = ChunkedPrefillEngine(cache, chunk_size=CH, num_heads=H, num_kv_heads=HKV, head_dim=D)
+    embc, wqc, wkc, wvc = emb.cuda(), wq.cuda(), wk.cuda(), wv.cuda()
+
+    def rope(q, k, positions):
+        c, s_ = om.compute_rope(D, positions.view(1, -1).cpu(), 10000.0)
+        c, s_ = c[0].to(q.device), s_[0].to(q.device)
+        rot = lambda x: x * c + om.rotate_half(x) * s_
+        return rot(q), rot(k)
+
+    def layer(x, attn_fn):
+        q = (x @ wqc).view(-1, H, D).transpose(0, 1)
+        k = (x @ wkc).view(-1, HKV, D).transpose(0, 1)
+        v = (x @ wvc).view(-1, HKV, D).transpose(0, 1)
+        return attn_fn(q.contiguous(), k.contiguous(), v.contiguous())
+
+    taken = []
+    orig_alloc = cache.allocate_blocks
+    cache.allocate_blocks = lambda n: taken.extend(orig_alloc(n)) or taken[-n:]
+    out = eng.prefill(ids, lambda t: embc[t], rope, layer)
+    pool = cache.allocator.pool
+    bt = list(taken)
+    # reference: the whole prompt at once in float64 on the CPU
+    x = emb[ids].double()
+    pos = torch.arange(P)
+    c, s_ = om.compute_rope(D, pos.view(1, -1), 10000.0)
+    c, s_ = c[0].double(), s_[0].double()
+    q = (x @ wq.double()).view(P, H, D).transpose(0, 1)
+    k = (x @ wk.double()).view(P, HKV, D).transpose(0, 1)
+    v = (x @ wv.double()).view(P, HKV, D).transpose(0, 1)
+    q = q * c + om.rotate_half(q) * s_
+    k = k * c + om.rotate_half(k) * s_
+    last = P - (P - 1) // CH * CH
+    qs = q[:, P - last:]
+    kk = k.repeat_interleave(H // HKV, dim=0)
+    vv = v.repeat_interleave(H // HKV, dim=0)
+    sc = qs @ kk.transpose(1, 2) / D ** 0.5
+    mask = torch.arange(P).view(1, -1) > torch.arange(P - last, P).view(-1, 1)
+    sc = sc.masked_fill(mask, float("-inf"))
+    ref = torch.softmax(sc, dim=-1) @ vv
+    assert rel_l2(out.cpu().numpy(), ref.numpy()) < 1e-5
+    # the pool holds every position's K and V in every layer of its block
+    got_k = torch.stack([pool[bt[p // B], :, 0, :, p % B, :] for p in range(P)], dim=0).cpu()
+    assert rel_l2(got_k[:, 0].transpose(0, 1).numpy(), k.numpy()) < 1e-5
+    assert torch.equal(got_k[:, 0], got_k[:, 1])
+    got_v = torch.stack([pool[bt[p // B], 1, 1, :, p % B, :] for p in range(P)], dim=1).cpu()
+    assert rel_l2(got_v.numpy(), v.numpy()) < 1e-5

@@ -232,3 +232,36 @@ def test_run_batch_mixed_prefill_and_decode_vs_oracle(tiny_sd):
     ref_b = om.generate(pb, 1)
     assert [ta[0], out[0]] == ref_a
     assert out[1] == ref_b[0]
+
+
+def test_preempted_request_resumes_with_generate_tokens(tiny_sd):
+    """A decoding request is swapped out (asynchronous device-to-host copy on
+    a side stream), its freed blocks are overwritten by later work on the
+    main stream, and after re-admission (host-to-device copy into its new
+    blocks) it finishes with the tokens generate() gives it alone."""
+    from kshipra_b200.continuous import ContinuousEngine, SeqState
+    from kshipra_b200.prefix_cache import PrefixCache
+    km = KshipraModel(config=TINY_LLAMA, state_dict=tiny_sd, quantize="int8")
+    cfg = km.cfg
+    g = torch.Generator().manual_seed(13)
+    pa = torch.randint(0, cfg.vocab, (37,), generator=g).tolist()
+    pb = torch.randint(0, cfg.vocab, (21,), generator=g).tolist()
+    cache = PrefixCache(32, 16, cfg.layers, cfg.kv_heads, cfg.head_dim, dtype=torch.float32,
+                        device=torch.device("cuda"))
+    eng = ContinuousEngine(cache, block_size=16, max_batch_tokens=64, itl_budget_s=0.064,
+                           t_tok_s=1e-3, model=km)
+    ra, rb = eng.add_request(pa, 9), eng.add_request(pb, 9)
+    while len(ra.generated_tokens) < 4:
+        eng.step()
+    assert ra.state == SeqState.RUNNING
+    freed = list(ra._own_blocks)
+    eng._preempt(ra)
+    assert ra.state == SeqState.WAITING and ra.swapped_kv is not None and freed
+    # later work on the main stream overwrites the freed blocks
+    cache.allocator.pool[torch.tensor(freed, device="cuda")] = float("nan")
+    for _ in range(1000):
+        if ra in eng.finished and rb in eng.finished:
+            break
+        eng.step()
+    assert ra.generated_tokens == km.generate(pa, max_new_tokens=9, block_size=16)
+    assert rb.generated_tokens == km.generate(pb, max_new_tokens=9, block_size=16)

@@ -89,3 +89,24 @@ def test_oracle_05b_prefill_matches_reference(golden):
     assert toks == g["int8/tokens"][:3].tolist()
     ref = g["int8/logits0"]
     assert np.abs(logs[0].numpy() - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_oracle_llama8b_l2_matches_reference(golden):
+    """Llama-3-8B shape cut to two layers, INT4: one short batch prompt, two tokens."""
+    g = golden("model_llama8b_l2.npz")
+    cfg = cases.llama8b_l2()
+    sd = synthetic_state_dict(cfg, seed=0)
+    assert weights_checksum(sd) == pytest.approx(float(g["weights_checksum"]), rel=1e-12)
+    om = OracleModel(cfg, sd, "int4")
+    del sd
+    p = cases.llama8b_batch_prompts(cfg.vocab)[4]
+    assert om.generate(p, 2, block_size=16) == g["int4/batch4/tokens"][:2].tolist()
+
+
+def test_oracle_cb_request_matches_reference(golden):
+    """A shortened config-3 request (system prefix + trace suffix), INT4 0.5B, two tokens."""
+    g = golden("model_cb_requests.npz")
+    sd = synthetic_state_dict(QWEN25_05B, seed=0)
+    om = OracleModel(QWEN25_05B, sd, "int4")
+    p = cases.cb_requests(QWEN25_05B.vocab)[1]
+    assert om.generate(p, 2, block_size=16) == g["req1/tokens"][:2].tolist()

@@ -4,7 +4,9 @@ skipped otherwise).
 The sharded model must give the unsharded model's greedy tokens (CUDA-graph
 decode with the all-reduces inside) and its logits within the 1e-3 relative
 bound: the row-parallel partial sums are added in a different order, which
-only moves the fp32 rounding.
+only moves the fp32 rounding.  At the Llama-3-8B shape (two layers, INT4
+and INT8) the sharded model is also checked against the reference's own
+tokens and logits (tests/golden/model_llama8b_l2.npz).
 """
 
 import os
@@ -25,8 +27,14 @@ def _free_port():
 
 
 def _cases():
-    from kshipra_b200.config import LLAMA3_8B, TINY_LLAMA, truncated
-    return [("tiny", TINY_LLAMA, "int8", 40, 12), ("8b-2l", truncated(LLAMA3_8B, 2), "int4", 48, 6)]
+    from kshipra_b200.config import TINY_LLAMA
+    return [("tiny", TINY_LLAMA, "int8", 40, 12)]
+
+
+def _golden_8b():
+    import numpy as np
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "model_llama8b_l2.npz")
+    return dict(np.load(path))
 
 
 def _worker(rank, world, port, out):
@@ -35,8 +43,9 @@ def _worker(rank, world, port, out):
     dev = torch.device("cuda", rank)
     import datetime
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
-                            timeout=datetime.timedelta(seconds=120))
+                            timeout=datetime.timedelta(seconds=300))
     try:
+        import cases
         from kshipra_b200.model import KshipraModel
         from kshipra_b200.weights import synthetic_state_dict
         res = {}
@@ -65,6 +74,36 @@ def _worker(rank, world, port, out):
             del sd
             torch.cuda.synchronize()
             dist.barrier()
+        # the 8B shape (two layers) against the reference's outputs, on the
+        # CPU-generated weights the fixtures were made from
+        g = _golden_8b()
+        cfg = cases.llama8b_l2()
+        sd = synthetic_state_dict(cfg, seed=0)
+        prompt = g["prompt"].tolist()
+        B = 16
+        for q in ("int4", "int8"):
+            tp = KshipraModel(config=cfg, state_dict=sd, quantize=q, device=dev,
+                              tp=(rank, world, None))
+            toks = tp.generate(prompt, max_new_tokens=cases.L8B_NEW, block_size=B,
+                               prefill_chunk=cases.L8B_CHUNK)
+            alloc = tp.new_pool((len(prompt) + B - 1) // B, B)
+            bt = list(range(alloc.pool.shape[0]))
+            pos = 0
+            while pos < len(prompt):
+                c = min(cases.L8B_CHUNK, len(prompt) - pos)
+                lg = tp.forward(torch.tensor([prompt[pos:pos + c]]),
+                                torch.arange(pos, pos + c).view(1, -1), alloc.pool, bt,
+                                list(range(pos, pos + c)), pos)
+                pos += c
+            lg = lg[0, -1].cpu().double()
+            ref = torch.from_numpy(g[f"{q}/logits_first"]).double()
+            err = float((lg - ref).abs().max() / ref.abs().max())
+            tp._gen_cache.clear()
+            del tp, alloc
+            torch.cuda.synchronize()
+            dist.barrier()
+            if rank == 0:
+                res[f"8b-2l-{q}"] = (toks, g[f"{q}/tokens"].tolist(), err)
         if rank == 0:
             out.update(res)
     finally:
@@ -74,8 +113,14 @@ def _worker(rank, world, port, out):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_tensor_parallel_two_gpus_matches_single_gpu():
     out = mp.get_context("spawn").Manager().dict()
+    import sys
+    golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    if golden not in sys.path:
+        sys.path.insert(0, golden)
+    os.environ["PYTHONPATH"] = os.pathsep.join(
+        [golden, os.path.dirname(golden)] + [p for p in os.environ.get("PYTHONPATH", "").split(os.pathsep) if p])
     mp.spawn(_worker, args=(2, _free_port(), out), nprocs=2, join=True)
-    assert set(out.keys()) == {name for name, *_ in _cases()}
+    assert set(out.keys()) == {name for name, *_ in _cases()} | {"8b-2l-int4", "8b-2l-int8"}
     for name, (toks, ref, err) in out.items():
         assert toks == ref, (name, toks, ref)
         assert err < 1e-3, (name, err)

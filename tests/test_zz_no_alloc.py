@@ -70,3 +70,10 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     st = h.ksh_lm_head_argmax_noalloc(x.data_ptr(), 17, 64, None, 0.0, w.data_ptr(), 1000, None,
                                       tok.data_ptr(), _lib.stream_ptr())
     assert st == TOO_LARGE
+
+
+def test_noalloc_scratch_covers_this_gpus_argmax_grid():
+    """The largest argmax grid on this GPU (8 CTAs per SM) fits the array for 16 rows."""
+    from kshipra_b200 import _lib
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert 256 + sms * 8 * 16 * 8 <= _lib.lib().ksh_lm_head_argmax_noalloc_max_bytes()
