@@ -226,20 +226,18 @@ def time_linear_family(km, T, reps=20):
 
 
 def time_lm_head(km, T, reps=30):
-    """The fused final norm + fp32 lm_head + argmax at T rows, launched alone."""
-    from kshipra_b200 import _lib as L
+    """The fused final norm + fp32 lm_head + argmax at T rows, launched alone
+    (the model's own call: the GEMV up to 16 rows, the tensor-core kernel on
+    the split weight above)."""
     dev = km.device
     x = torch.randn((T, km.hidden), device=dev)
     tok = torch.empty(T, dtype=torch.int64, device=dev)
-    ws = torch.empty(int(L.lib().ksh_lm_head_workspace_size(T, km.tp.vocab)), dtype=torch.uint8,
-                     device=dev)
+    ws = torch.empty(km.lm_ws_bytes(T), dtype=torch.uint8, device=dev)
     lg = km._tp_logits(T) if km.tp_world > 1 else None
     stream = torch.cuda.current_stream()
 
     def once():
-        L.call("ksh_lm_head_argmax", x.data_ptr(), T, km.hidden, km.norm_w.data_ptr(), km.eps,
-               km.lm_head.data_ptr(), km.tp.vocab, None if lg is None else lg.data_ptr(),
-               tok.data_ptr(), ws.data_ptr(), ws.numel(), L.stream_ptr())
+        km._lm_head_call(x, T, lg, tok, ws)
     for _ in range(3):
         once()
     r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -844,7 +842,8 @@ def run_tp(args, wl):
             "batched-decode quantized linears of one step at 64 rows (q/k/v, o, gate/up + "
             "SwiGLU, down; all layers, one CUDA-graph replay)", lin_bytes, lin_ms, hbm, peak_kind),
         roofline_lm_head=roofline_entry(
-            "batch lm_head + argmax at 64 rows (ksh_lm_head_argmax, vocabulary shard)",
+            "batch lm_head + argmax at 64 rows (ksh_lm_head_argmax_tc on the split fp16 weight, "
+            "vocabulary shard)",
             lm_bytes, lm_ms, hbm, peak_kind),
         gpu_launches=args.steps * per_step,
         clocks=clk.summary(),

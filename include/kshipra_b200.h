@@ -236,6 +236,24 @@ int64_t ksh_lm_head_argmax_noalloc_max_bytes(void);
 int ksh_lm_head_argmax_noalloc(const float* x, int64_t m, int64_t hidden, const float* norm_w,
                                float norm_eps, const float* w, int64_t vocab, float* logits,
                                int64_t* tokens, void* stream);
+/* The same lm_head (+ argmax) on tcgen05 tensor cores for many rows (the
+ * decode step of a large batch, the L-row logits of a prefill forward).
+ * The fp32 weight is split once by ksh_lm_head_split_weight into fp16
+ * w_hi, w_lo [vocab, hidden] and w_inv [vocab] (per row a power-of-two
+ * scale 2^s with max|w| * 2^s in [2^14, 2^15): w * 2^s = hi + lo, w_inv =
+ * 2^-s; non-finite weights raise KSH_FLAG_NONFINITE in *flags).  Each call
+ * splits x the same way (RMSNorm folded in) and runs W_hi x (x_hi + x_lo) +
+ * W_lo x x_hi with fp32 accumulation, so only the lo x lo term (about 2^-22
+ * of each product) is dropped.  Any m (64 rows per launch, one pass over the
+ * weight each); hidden % 8 == 0; 16-byte aligned w_hi / w_lo; workspace of
+ * ksh_lm_head_tc_workspace_size(m, hidden, vocab) bytes, 256-byte aligned. */
+int64_t ksh_lm_head_tc_workspace_size(int64_t m, int64_t hidden, int64_t vocab);
+int ksh_lm_head_split_weight(const float* w, int64_t vocab, int64_t hidden, void* w_hi,
+                             void* w_lo, float* w_inv, int32_t* flags, void* stream);
+int ksh_lm_head_argmax_tc(const float* x, int64_t m, int64_t hidden, const float* norm_w,
+                          float norm_eps, const void* w_hi, const void* w_lo, const float* w_inv,
+                          int64_t vocab, float* logits, int64_t* tokens, void* workspace,
+                          int64_t workspace_bytes, void* stream);
 /* Row-wise argmax of materialised logits [m, vocab]. */
 int ksh_argmax_rows(const float* logits, int64_t m, int64_t vocab, int64_t* out,
                     void* stream);

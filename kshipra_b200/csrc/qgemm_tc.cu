@@ -476,9 +476,120 @@ split_x_kernel(const float* __restrict__ x, int64_t k, __half* __restrict__ xh,
   }
 }
 
+// The same split, vectorised for k % 8 == 0 and k <= 8 * kSxChunks * kSxThreads:
+// each thread loads its 8-element chunks once (two float4 each) and keeps them
+// in registers for both passes; 16 warps per row; hi and lo leave as one
+// 16-byte store per chunk.  Results equal split_x_kernel's up to the order of
+// the row reductions (fixed here too).
+constexpr int kSxThreads = 512;
+constexpr int kSxChunks = 4;
+
+template <bool PERM>
+__global__ void __launch_bounds__(kSxThreads)
+split_x_vec_kernel(const float* __restrict__ x, int64_t k, __half* __restrict__ xh,
+                   __half* __restrict__ xl, float* __restrict__ inv_row,
+                   const float* __restrict__ norm_w, float eps) {
+  __shared__ float red[2][kSxThreads / 32];
+  grid_dep_wait();
+  grid_dep_launch();
+  const int64_t r = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + r * k);
+  const float4* nw4 = reinterpret_cast<const float4*>(norm_w);
+  const int nchunk = static_cast<int>(k / 8);
+  float v[kSxChunks][8];
+  float ss = 0.0f, mx = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kSxChunks; ++j) {
+    const int c = threadIdx.x + j * kSxThreads;
+    if (c < nchunk) {
+      const float4 a0 = xr[2 * c], a1 = xr[2 * c + 1];
+      v[j][0] = a0.x; v[j][1] = a0.y; v[j][2] = a0.z; v[j][3] = a0.w;
+      v[j][4] = a1.x; v[j][5] = a1.y; v[j][6] = a1.z; v[j][7] = a1.w;
+      float w8[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+      if (norm_w) {
+        const float4 b0 = nw4[2 * c], b1 = nw4[2 * c + 1];
+        w8[0] = b0.x; w8[1] = b0.y; w8[2] = b0.z; w8[3] = b0.w;
+        w8[4] = b1.x; w8[5] = b1.y; w8[6] = b1.z; w8[7] = b1.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        ss = fmaf(v[j][e], v[j][e], ss);
+        mx = fmaxf(mx, fabsf(norm_w ? w8[e] * v[j][e] : v[j][e]));
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  mx = warp_max(mx);
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = ss;
+    red[1][threadIdx.x >> 5] = mx;
+  }
+  __syncthreads();
+  ss = 0.0f;
+  mx = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kSxThreads / 32; ++w) {     // fixed order
+    ss += red[0][w];
+    mx = fmaxf(mx, red[1][w]);
+  }
+  float inv = 1.0f;
+  if (norm_w) {
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(k)), eps)));
+    mx *= inv;
+  }
+  int e = 0;
+  if (mx > 0.0f && isfinite(mx)) {
+    int ex;
+    frexpf(mx, &ex);
+    e = max(-100, min(15 - ex, 100));
+  }
+  const float sc = ldexpf(1.0f, e);
+  if (threadIdx.x == 0) inv_row[r] = ldexpf(1.0f, -e);
+#pragma unroll
+  for (int j = 0; j < kSxChunks; ++j) {
+    const int c = threadIdx.x + j * kSxThreads;
+    if (c < nchunk) {
+      float w8[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+      if (norm_w) {
+        const float4 b0 = nw4[2 * c], b1 = nw4[2 * c + 1];
+        w8[0] = b0.x; w8[1] = b0.y; w8[2] = b0.z; w8[3] = b0.w;
+        w8[4] = b1.x; w8[5] = b1.y; w8[6] = b1.z; w8[7] = b1.w;
+      }
+      __align__(16) __half hv[8], lv[8];
+#pragma unroll
+      for (int el = 0; el < 8; ++el) {
+        const float nv = norm_w ? __fmul_rn(w8[el], __fmul_rn(v[j][el], inv)) : v[j][el];
+        const float t = nv * sc;
+        const __half h = __float2half_rn(t);
+        // PERM: element el of the chunk goes to position (el & 1) * 4 + (el >> 1)
+        const int pos = PERM ? ((el & 1) << 2) + (el >> 1) : el;
+        hv[pos] = h;
+        lv[pos] = __float2half_rn(t - __half2float(h));
+      }
+      *reinterpret_cast<uint4*>(xh + r * k + 8 * c) = *reinterpret_cast<const uint4*>(hv);
+      *reinterpret_cast<uint4*>(xl + r * k + 8 * c) = *reinterpret_cast<const uint4*>(lv);
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
+
+int launch_split(const float* x, int64_t m, int64_t k, __half* xh, __half* xl, float* inv,
+                 const float* norm_w, float eps, bool perm, cudaStream_t stream) {
+  const bool vec = k % 8 == 0 && k <= 8LL * kSxChunks * kSxThreads &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(norm_w) |
+                     reinterpret_cast<uintptr_t>(xh) | reinterpret_cast<uintptr_t>(xl)) & 15) == 0;
+  if (vec) {
+    auto kern = perm ? split_x_vec_kernel<true> : split_x_vec_kernel<false>;
+    return launch(kern, dim3(static_cast<unsigned>(m)), dim3(kSxThreads), 0, stream, x, k, xh,
+                  xl, inv, norm_w, eps);
+  }
+  auto kern = perm ? split_x_kernel<true> : split_x_kernel<false>;
+  return launch(kern, dim3(static_cast<unsigned>(m)), dim3(256), 0, stream, x, k, xh, xl, inv,
+                norm_w, eps);
+}
 
 
 int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
@@ -534,8 +645,7 @@ int launch_tc(const LinArgs& a, char* ws, cudaStream_t stream) {
   __half* xh = reinterpret_cast<__half*>(ws + L.xh);
   __half* xl = reinterpret_cast<__half*>(ws + L.xl);
   float* inv = reinterpret_cast<float*>(ws + L.inv);
-  int st = launch(split_x_kernel<false>, dim3(static_cast<unsigned>(a.m)), dim3(256), 0, stream, a.x,
-                  a.k, xh, xl, inv, a.norm_w, a.norm_eps);
+  int st = launch_split(a.x, a.m, a.k, xh, xl, inv, a.norm_w, a.norm_eps, false, stream);
   if (st != KSH_OK) return st;
   CUtensorMap mxh, mxl, mw;
   if (!make_tensor_map_2d(&mxh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, xh, a.k, a.m, a.k * 2, BK, BM,
@@ -598,9 +708,7 @@ int launch_split_x(const LinArgs& a, char* ws, bool perm, __half** xh, __half** 
   *xh = reinterpret_cast<__half*>(ws + L.xh);
   *xl = reinterpret_cast<__half*>(ws + L.xl);
   *inv = reinterpret_cast<float*>(ws + L.inv);
-  auto kern = perm ? split_x_kernel<true> : split_x_kernel<false>;
-  return launch(kern, dim3(static_cast<unsigned>(a.m)), dim3(256), 0, stream, a.x, a.k, *xh, *xl,
-                *inv, a.norm_w, a.norm_eps);
+  return launch_split(a.x, a.m, a.k, *xh, *xl, *inv, a.norm_w, a.norm_eps, perm, stream);
 }
 
 int64_t split_x_workspace_size(int64_t m, int64_t k) { return ws_layout(m, k, 0).total; }

@@ -47,6 +47,7 @@ FLAG_NAMES = {1: "non-finite weight", 2: "block id out of range", 4: "slot out o
               8: "position outside the RoPE table", 16: "token id out of range",
               32: "sequence longer than its block table", 64: "a bounded device wait gave up"}
 FLAG_TIMEOUT = 64
+LM_GEMV_ROWS = 16            # lm_head rows served by the fp32 GEMV; more go to tensor cores
 
 
 # GQA group sizes the fused decode-attention kernel is instantiated for, per head dim.
@@ -142,6 +143,8 @@ class KshipraModel:
         self._lin_ws = Workspace()
         self._attn_ws = AttentionWorkspace()
         self._lm_ws: Optional[torch.Tensor] = None
+        self._lm_hl = None
+        self.lm_tc = True            # > 16 lm_head rows on the tensor-core kernel
         self._gen_cache: Dict[tuple, tuple] = {}
         self.fused_decode = True
         with torch.cuda.device(self.device):
@@ -329,24 +332,61 @@ class KshipraModel:
         if self.tp_world > 1:
             torch.distributed.all_reduce(t, group=self.tp_group)
 
+    def lm_ws_bytes(self, m: int) -> int:
+        """Workspace bytes of the lm_head call for ``m`` rows."""
+        n = int(_lib.lib().ksh_lm_head_workspace_size(m, self.tp.vocab))
+        if m > LM_GEMV_ROWS and self.lm_tc:
+            n = max(n, int(_lib.lib().ksh_lm_head_tc_workspace_size(m, self.hidden, self.tp.vocab)))
+        return n
+
     def _lm_workspace(self, m: int) -> torch.Tensor:
-        need = int(_lib.lib().ksh_lm_head_workspace_size(m, self.vocab_size))
+        need = self.lm_ws_bytes(m)
         if self._lm_ws is None or self._lm_ws.numel() < need:
-            self._lm_ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+            self._lm_ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self._lm_ws
+
+    def lm_head_split(self):
+        """The lm_head weight (this rank's vocabulary rows) split once into
+        fp16 hi / lo terms with a power-of-two scale per row, for the
+        tensor-core lm_head of more than 16 rows (same 4 bytes per weight as
+        the fp32 copy, which the GEMV path keeps reading).  Made on first use;
+        callers that capture CUDA graphs make it before the capture."""
+        if self._lm_hl is None:
+            V, H = self.lm_head.shape
+            with torch.cuda.device(self.device):
+                hi = torch.empty((V, H), dtype=torch.float16, device=self.device)
+                lo = torch.empty((V, H), dtype=torch.float16, device=self.device)
+                inv = torch.empty(V, dtype=torch.float32, device=self.device)
+                call("ksh_lm_head_split_weight", ptr(self.lm_head), V, H, ptr(hi), ptr(lo),
+                     ptr(inv), ptr(self.flags), stream_ptr())
+                _check_flags(self.flags)
+            self._lm_hl = (hi, lo, inv)
+        return self._lm_hl
+
+    def _lm_head_call(self, x: torch.Tensor, m: int, logits: Optional[torch.Tensor],
+                      tokens: Optional[torch.Tensor], ws: torch.Tensor) -> None:
+        """Fused final norm + lm_head (+ argmax): a GEMV up to 16 rows, above
+        that the tensor-core kernel on the split weight (one pass over the
+        weight per 64 rows)."""
+        vl = self.tp.vocab
+        if m > LM_GEMV_ROWS and self.lm_tc:
+            hi, lo, inv = self.lm_head_split()
+            call("ksh_lm_head_argmax_tc", ptr(x), m, self.hidden, ptr(self.norm_w), self.eps,
+                 ptr(hi), ptr(lo), ptr(inv), vl, ptr(logits), ptr(tokens), ptr(ws), ws.numel(),
+                 stream_ptr())
+        else:
+            call("ksh_lm_head_argmax", ptr(x), m, self.hidden, ptr(self.norm_w), self.eps,
+                 ptr(self.lm_head), vl, ptr(logits), ptr(tokens), ptr(ws), ws.numel(),
+                 stream_ptr())
 
     def _lm_head_argmax(self, x: torch.Tensor, tokens: torch.Tensor,
                         ws: Optional[torch.Tensor] = None, logits: Optional[torch.Tensor] = None):
         m = x.shape[0]
         if ws is None:
             ws = self._lm_workspace(m)
-        vl = self.tp.vocab
         if self.tp_world > 1 and logits is None:
             logits = self._tp_logits(m)
-        # fused final norm + lm_head + argmax: a GEMV up to 16 rows, above that
-        # one pass over the weight per 64 rows
-        call("ksh_lm_head_argmax", ptr(x), m, self.hidden, ptr(self.norm_w), self.eps,
-             ptr(self.lm_head), vl, ptr(logits), ptr(tokens), ptr(ws), ws.numel(), stream_ptr())
+        self._lm_head_call(x, m, logits, tokens, ws)
         if self.tp_world > 1:
             # vocabulary-parallel: every rank's (max logit, global index), then
             # the first index of the overall maximum
@@ -390,8 +430,11 @@ class KshipraModel:
                                   pool, self._lin_ws, self._attn_ws)
             vl = self.tp.vocab
             logits = torch.empty((L, vl), dtype=torch.float32, device=dev)
-            linear_launch(xn, None, self.lm_head, None, logits, ws=self._lin_ws,
-                          norm_w=self.norm_w, eps=self.eps)
+            if L > LM_GEMV_ROWS and self.lm_tc:
+                self._lm_head_call(xn, L, logits, None, self._lm_workspace(L))
+            else:
+                linear_launch(xn, None, self.lm_head, None, logits, ws=self._lin_ws,
+                              norm_w=self.norm_w, eps=self.eps)
             if self.tp_world > 1:           # vocabulary shards -> full rows
                 parts = torch.empty((self.tp_world, L, vl), dtype=torch.float32, device=dev)
                 torch.distributed.all_gather_into_tensor(parts, logits, group=self.tp_group)
@@ -588,8 +631,9 @@ class DecodeState:
         nbytes = int(_lib.lib().ksh_paged_attention_workspace_size(
             B, model.n_heads, model.n_kv_heads, model.head_dim, 1, self.capacity))
         self.attn_ws.get(nbytes, dev)
-        self.lm_ws = torch.zeros(int(_lib.lib().ksh_lm_head_workspace_size(B, model.vocab_size)),
-                                 dtype=torch.uint8, device=dev)
+        self.lm_ws = torch.empty(model.lm_ws_bytes(B), dtype=torch.uint8, device=dev)
+        if B > LM_GEMV_ROWS and model.lm_tc:
+            model.lm_head_split()        # before any graph capture of the step
         self.graph: Optional[torch.cuda.CUDAGraph] = None
 
     def start(self, first_tokens: torch.Tensor, prompt_lens: List[int]) -> None:

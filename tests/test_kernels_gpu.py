@@ -834,3 +834,81 @@ def test_chunked_prefill_engine_mock_layer_vs_cpu():
     assert torch.equal(got_k[:, 0], got_k[:, 1])
     got_v = torch.stack([pool[bt[p // B], 1, 1, :, p % B, :] for p in range(P)], dim=1).cpu()
     assert rel_l2(got_v.numpy(), v.numpy()) < 1e-5
+
+
+@pytest.mark.parametrize("m,H,V,norm", [(17, 4096, 128256, True), (64, 4096, 128256, False),
+                                        (65, 896, 1000, True), (130, 256, 130, False),
+                                        (20, 896, 151936, True), (1, 512, 777, False)])
+def test_lm_head_tensor_core_split_weight(m, H, V, norm):
+    """ksh_lm_head_argmax_tc on the split fp16 weight: logits within 1e-5 of
+    the largest |logit| of a float64 reference (the other lm_head paths'
+    bound), tokens the first index of the maximum of those logits (a tie
+    between duplicate weight rows goes to the lower index), more than 64 rows
+    in several launches, a workspace that starts as 0xFF bytes and no write
+    past the size the query asked for."""
+    from kshipra_b200 import _lib
+    gen = torch.Generator().manual_seed(m * 13 + H + V)
+    w = torch.randn((V, H), generator=gen) * 0.02
+    w[V // 3] = w[V - 5]
+    x = torch.randn((m, H), generator=gen)
+    x[0] = w[V - 5] * 50
+    nw = 1.0 + 0.1 * torch.randn(H, generator=gen)
+    wc, xc, nc = w.cuda(), x.cuda(), nw.cuda()
+    hi = torch.empty((V, H), dtype=torch.float16, device="cuda")
+    lo = torch.empty_like(hi)
+    inv = torch.empty(V, device="cuda")
+    flags = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _lib.call("ksh_lm_head_split_weight", wc.data_ptr(), V, H, hi.data_ptr(), lo.data_ptr(),
+              inv.data_ptr(), flags.data_ptr(), _lib.stream_ptr())
+    # the split reconstructs the weight to about 2^-22 of each row's maximum
+    rec = (hi.double() + lo.double()) * inv.double().view(-1, 1)
+    err = (rec.cpu() - w.double()).abs().max(dim=1).values / w.double().abs().max(dim=1).values
+    assert float(err.max()) < 2.0 ** -21 and int(flags.item()) == 0
+    need = int(_lib.lib().ksh_lm_head_tc_workspace_size(m, H, V))
+    guard = 1 << 16
+    ws = torch.full((need + guard,), 0xFF, dtype=torch.uint8, device="cuda")
+    ws[need:] = 0xAB
+    logits = torch.empty((m, V), device="cuda")
+    tok = torch.full((m,), -7, dtype=torch.int64, device="cuda")
+    xd = x.double()
+    if norm:
+        xd = xd * torch.rsqrt(xd.pow(2).mean(-1, keepdim=True) + 1e-6) * nw.double()
+    ref = xd @ w.double().T
+    for _ in range(2):
+        _lib.call("ksh_lm_head_argmax_tc", xc.data_ptr(), m, H, nc.data_ptr() if norm else None,
+                  1e-6, hi.data_ptr(), lo.data_ptr(), inv.data_ptr(), V, logits.data_ptr(),
+                  tok.data_ptr(), ws.data_ptr(), need, _lib.stream_ptr())
+        torch.cuda.synchronize()
+        assert bool((ws[need:] == 0xAB).all())
+        lg = logits.cpu()
+        assert float((lg.double() - ref).abs().max()) <= 1e-5 * float(ref.abs().max())
+        assert tok.cpu().tolist() == torch.argmax(lg, dim=1).tolist()
+        assert int(tok[0]) == V // 3
+    # argmax only (no logits buffer) gives the same tokens
+    tok2 = torch.full((m,), -7, dtype=torch.int64, device="cuda")
+    _lib.call("ksh_lm_head_argmax_tc", xc.data_ptr(), m, H, nc.data_ptr() if norm else None, 1e-6,
+              hi.data_ptr(), lo.data_ptr(), inv.data_ptr(), V, None, tok2.data_ptr(),
+              ws.data_ptr(), need, _lib.stream_ptr())
+    torch.cuda.synchronize()
+    assert tok2.cpu().tolist() == tok.cpu().tolist()
+
+
+def test_model_lm_head_paths_agree():
+    """The model's lm_head above 16 rows (tensor cores, split weight) and the
+    fp32 GEMV path give the same tokens and logits within 1e-5."""
+    from kshipra_b200.config import TINY_LLAMA
+    from kshipra_b200.model import KshipraModel
+    from kshipra_b200.weights import synthetic_state_dict
+    km = KshipraModel(config=TINY_LLAMA, state_dict=synthetic_state_dict(TINY_LLAMA, seed=0),
+                      quantize="int8")
+    x = torch.randn((40, TINY_LLAMA.hidden), device="cuda")
+    lg_tc = torch.empty((40, TINY_LLAMA.vocab), device="cuda")
+    tok_tc = torch.empty(40, dtype=torch.int64, device="cuda")
+    km._lm_head_argmax(x, tok_tc, logits=lg_tc)
+    km.lm_tc = False
+    lg_f = torch.empty_like(lg_tc)
+    tok_f = torch.empty_like(tok_tc)
+    km._lm_head_argmax(x, tok_f, logits=lg_f)
+    scale = float(lg_f.abs().max())
+    assert float((lg_tc - lg_f).abs().max()) <= 1e-5 * scale
+    assert tok_tc.tolist() == tok_f.tolist()
