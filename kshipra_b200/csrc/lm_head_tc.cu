@@ -18,6 +18,9 @@
 //   TMEM tile: W_hi x [x_hi | x_lo] (N = 128: columns 0..63 take x_hi, 64..127
 //   x_lo) and W_lo x x_hi (N = 64, into columns 0..63).  Only lo * lo (about
 //   2^-22 of the product) is dropped; logit = (col c + col 64 + c) * 2^-s * 2^-e;
+// * each K chunk of 256 goes to a fresh (double-buffered) TMEM accumulator
+//   and the epilogue warps add the chunks in fp32 registers, so no tensor-core
+//   accumulation chain is longer than 16 MMA steps;
 // * swap-AB: vocabulary rows are the MMA's M side (TMEM lanes), the 64 batch
 //   rows (zero-filled by TMA past m) its N side;
 // * persistent CTAs (one per SM) loop over vocabulary tiles; warp 0 streams
@@ -63,6 +66,7 @@ constexpr int BAR_OFF = RING;
 constexpr int SMEM = 1024 + RING + 1024;
 constexpr uint32_t TMEM_COLS = 2 * 2 * MP;   // two buffers of [x_hi cols | x_lo cols]
 constexpr uint32_t kPolls = 1u << 22;
+constexpr int PROMO = 4;                // K stages per TMEM accumulator chunk (K = 256)
 
 struct TcArgs {
   const float* x_inv;      // [m_total] 2^-e per batch row (split_x), rows r0 ..
@@ -207,38 +211,46 @@ lm_tc_kernel(const __grid_constant__ CUtensorMap map_wh, const __grid_constant__
       constexpr uint32_t idesc_hl = idesc_f16_f32(BV, 2 * MP);   // W_hi x [x_hi | x_lo]
       constexpr uint32_t idesc_h = idesc_f16_f32(BV, MP);        // W_lo x x_hi
       int q = 0;
-      for (int t = 0; t < my_tiles && !*abort_flag; ++t) {
-        const int buf = t & 1;
-        if (t >= 2 && !mbar_wait(&acc_empty[buf], ((t >> 1) - 1) & 1, kPolls)) {
-          *abort_flag = 1;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d = tmem + static_cast<uint32_t>(buf * 2 * MP);
-        bool ok = true;
-        for (int kk = 0; kk < kt; ++kk, ++q) {
-          const int s = q % NS;
-          if (*abort_flag || !mbar_wait(&full[s], (q / NS) & 1, kPolls)) {
+      // The tile's K range runs in chunks of PROMO stages, each into a fresh
+      // TMEM accumulator (double-buffered); the epilogue adds the chunks in
+      // fp32 registers.  The tensor core's accumulation over a long K chain
+      // loses low bits (measured: 3e-5 of the largest logit over K = 4096 in
+      // one accumulator); over 16 MMA steps per chunk it stays near 1e-6.
+      const int nch = (kt + PROMO - 1) / PROMO;
+      int g = 0;
+      bool ok = true;
+      for (int t = 0; t < my_tiles && ok; ++t) {
+        for (int ch = 0; ch < nch && ok; ++ch, ++g) {
+          const int buf = g & 1;
+          if (*abort_flag || (g >= 2 && !mbar_wait(&acc_empty[buf], ((g >> 1) - 1) & 1, kPolls))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t ah = desc_k_sw128(smem_u32(wh_tile(s)));
-          const uint64_t al = desc_k_sw128(smem_u32(wl_tile(s)));
-          const uint64_t bx = desc_k_sw128(smem_u32(xh_tile(s)));
+          const uint32_t d = tmem + static_cast<uint32_t>(buf * 2 * MP);
+          const int k_end = min(kt, (ch + 1) * PROMO);
+          for (int kk = ch * PROMO; kk < k_end; ++kk, ++q) {
+            const int s = q % NS;
+            if (*abort_flag || !mbar_wait(&full[s], (q / NS) & 1, kPolls)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint64_t ah = desc_k_sw128(smem_u32(wh_tile(s)));
+            const uint64_t al = desc_k_sw128(smem_u32(wl_tile(s)));
+            const uint64_t bx = desc_k_sw128(smem_u32(xh_tile(s)));
 #pragma unroll
-          for (int k16 = 0; k16 < BK / 16; ++k16) {
-            mma_f16(d, ah + 2 * k16, bx + 2 * k16, idesc_hl, (kk > 0 || k16 > 0) ? 1u : 0u);
-            mma_f16(d, al + 2 * k16, bx + 2 * k16, idesc_h, 1u);
+            for (int k16 = 0; k16 < BK / 16; ++k16) {
+              mma_f16(d, ah + 2 * k16, bx + 2 * k16, idesc_hl,
+                      (kk > ch * PROMO || k16 > 0) ? 1u : 0u);
+              mma_f16(d, al + 2 * k16, bx + 2 * k16, idesc_h, 1u);
+            }
+            mma_commit(&empty[s]);
           }
-          mma_commit(&empty[s]);
+          if (ok) mma_commit(&acc_full[buf]);
         }
-        if (!ok) {
-          *abort_flag = 1;
-          break;
-        }
-        mma_commit(&acc_full[buf]);
       }
+      if (!ok) *abort_flag = 1;
       // every MMA of this thread completes before the TMEM is released
       mma_commit(drained);
       mbar_wait(drained, 0, kPolls);
@@ -254,27 +266,39 @@ lm_tc_kernel(const __grid_constant__ CUtensorMap map_wh, const __grid_constant__
     epi_bar_or(false);
     uint32_t best_key = 0u;                          // thread et < m keeps batch row et
     int32_t best_idx = INT32_MAX;
-    for (int t = 0; t < my_tiles; ++t) {
-      const int buf = t & 1;
+    const int nch = (kt + PROMO - 1) / PROMO;
+    int g = 0;
+    bool ok = true;
+    for (int t = 0; t < my_tiles && ok; ++t) {
       const int tile = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
-      // all 128 threads agree on giving up, so none is left at a barrier
-      const bool fail = *abort_flag || !mbar_wait(&acc_full[buf], (t >> 1) & 1, kPolls);
-      if (epi_bar_or(fail)) {
-        *abort_flag = 1;
-        break;
+      // columns 0..63: W_hi x_hi + W_lo x_hi; 64..127: W_hi x_lo, summed over
+      // the tile's K chunks in registers
+      float acc[MP];
+#pragma unroll
+      for (int c = 0; c < MP; ++c) acc[c] = 0.0f;
+      for (int ch = 0; ch < nch; ++ch, ++g) {
+        const int buf = g & 1;
+        // all 128 threads agree on giving up, so none is left at a barrier
+        const bool fail = *abort_flag || !mbar_wait(&acc_full[buf], (g >> 1) & 1, kPolls);
+        if (epi_bar_or(fail)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t taddr = tmem + static_cast<uint32_t>(buf * 2 * MP) + (static_cast<uint32_t>(quad * 32) << 16);
+#pragma unroll
+        for (int half = 0; half < MP / 32; ++half) {
+          float vh[32], vl[32];                      // valid only after tcgen05.wait::ld
+          tmem_ld_32x32b_x32(taddr + half * 32, vh);
+          tmem_ld_32x32b_x32(taddr + MP + half * 32, vl);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) acc[half * 32 + e] += vh[e] + vl[e];
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);                // the accumulator may be overwritten
       }
-      tc_fence_after();
-      const uint32_t taddr = tmem + static_cast<uint32_t>(buf * 2 * MP) + (static_cast<uint32_t>(quad * 32) << 16);
-      // columns 0..63: W_hi x_hi + W_lo x_hi; 64..127: W_hi x_lo (registers
-      // are valid only after tcgen05.wait::ld)
-      float h0[32], h1[32], l0[32], l1[32];
-      tmem_ld_32x32b_x32(taddr, h0);
-      tmem_ld_32x32b_x32(taddr + 32, h1);
-      tmem_ld_32x32b_x32(taddr + MP, l0);
-      tmem_ld_32x32b_x32(taddr + MP + 32, l1);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);                  // the accumulator may be overwritten
+      if (!ok) break;
       const int v = tile * BV + row;
       const bool live = v < a.vocab;
       const float winv = live ? a.w_inv[v] : 0.0f;
@@ -282,8 +306,7 @@ lm_tc_kernel(const __grid_constant__ CUtensorMap map_wh, const __grid_constant__
 #pragma unroll
       for (int c = 0; c < MP; ++c) {
         if (c < a.m) {
-          const float sum = c < 32 ? h0[c & 31] + l0[c & 31] : h1[c & 31] + l1[c & 31];
-          const float val = sum * (winv * xinv_s[c]);
+          const float val = acc[c] * (winv * xinv_s[c]);
           if (a.logits && live) a.logits[static_cast<int64_t>(c) * a.vocab + v] = val;
           const uint32_t key = live ? fkey(val) : 0u;
           const uint32_t wmax = __reduce_max_sync(0xffffffffu, key);
@@ -309,6 +332,7 @@ lm_tc_kernel(const __grid_constant__ CUtensorMap map_wh, const __grid_constant__
       // candidates of tile t + 1 go to the other buffer; tile t + 2 reuses
       // this one only after the next barrier
     }
+    if (!ok) *abort_flag = 1;
     if (a.tokens && et < a.m) {
       a.part_key[static_cast<int64_t>(blockIdx.x) * MP + et] = best_key;
       a.part_idx[static_cast<int64_t>(blockIdx.x) * MP + et] = best_idx;
