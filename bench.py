@@ -603,55 +603,58 @@ def run_micro(args):
     ws = Workspace()
     flt = args.micro_filter.split(",") if args.micro_filter else None
     results = []
-    for scheme in ("int4", "int8"):
-        for (k, n) in MICRO_SHAPES:
-            for m in MICRO_M:
-                tag = f"{scheme}:{m}:{k}x{n}"
-                if flt and tag not in flt:
-                    continue
-                qw, x, y = micro_case(scheme, m, k, n, dev)
-                # Enough weight copies that one pass over them exceeds twice the
-                # L2, so every launch streams its weights from HBM; the launches
-                # replay from a CUDA graph, so host overhead is not timed.
-                ncopy = max(1, min(64, -(-300_000_000 // qw.storage_bytes())))
-                if m > 64:
-                    ncopy = 1
-                copies = [qw] + [dataclasses.replace(qw, payload=qw.payload.clone(),
-                                                     scales=qw.scales.clone())
-                                 for _ in range(ncopy - 1)]
+    points = [(sc, m, k, n) for sc in ("int4", "int8") for (k, n) in MICRO_SHAPES for m in MICRO_M]
+    if flt:
+        # any scheme:M:KxN point, also M outside the sweep (e.g. a 2048-row prefill chunk)
+        points = []
+        for tag in flt:
+            sc, m, kn = tag.split(":")
+            k, n = kn.split("x")
+            points.append((sc, int(m), int(k), int(n)))
+    for scheme, m, k, n in points:
+        qw, x, y = micro_case(scheme, m, k, n, dev)
+        # Enough weight copies that one pass over them exceeds twice the
+        # L2, so every launch streams its weights from HBM; the launches
+        # replay from a CUDA graph, so host overhead is not timed.
+        ncopy = max(1, min(64, -(-300_000_000 // qw.storage_bytes())))
+        if m > 64:
+            ncopy = 1
+        copies = [qw] + [dataclasses.replace(qw, payload=qw.payload.clone(),
+                                             scales=qw.scales.clone())
+                         for _ in range(ncopy - 1)]
+        for c in copies:
+            linear_launch(x, c, None, None, y, ws=ws)
+        torch.cuda.synchronize()
+        if args.profile:
+            torch.cuda.cudart().cudaProfilerStart()
+            linear_launch(x, qw, None, None, y, ws=ws)
+            torch.cuda.synchronize()
+            torch.cuda.cudart().cudaProfilerStop()
+            continue
+        rounds = max(1, 64 // ncopy) if m <= 64 else 3
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(rounds):
                 for c in copies:
                     linear_launch(x, c, None, None, y, ws=ws)
-                torch.cuda.synchronize()
-                if args.profile:
-                    torch.cuda.cudart().cudaProfilerStart()
-                    linear_launch(x, qw, None, None, y, ws=ws)
-                    torch.cuda.synchronize()
-                    torch.cuda.cudart().cudaProfilerStop()
-                    continue
-                rounds = max(1, 64 // ncopy) if m <= 64 else 3
-                graph = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(graph):
-                    for _ in range(rounds):
-                        for c in copies:
-                            linear_launch(x, c, None, None, y, ws=ws)
-                for _ in range(3):
-                    graph.replay()
-                torch.cuda.synchronize()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
-                graph.replay()
-                e1.record()
-                torch.cuda.synchronize()
-                us = e0.elapsed_time(e1) * 1e3 / (rounds * ncopy)
-                del graph, copies
-                wbytes = qw.storage_bytes()
-                nbytes = wbytes + m * k * 4 + m * n * 4
-                flops = 2.0 * m * n * k
-                results.append({"scheme": scheme, "m": m, "k": k, "n": n, "us": us,
-                                "gb_s": nbytes / us / 1e3, "hbm_frac": nbytes / us / 1e3 / hbm,
-                                "tflop_s": flops / us / 1e6,
-                                "tensor_frac": flops / us / 1e6 / tc_peak})
-                del qw, x, y
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (rounds * ncopy)
+        del graph, copies
+        wbytes = qw.storage_bytes()
+        nbytes = wbytes + m * k * 4 + m * n * 4
+        flops = 2.0 * m * n * k
+        results.append({"scheme": scheme, "m": m, "k": k, "n": n, "us": us,
+                        "gb_s": nbytes / us / 1e3, "hbm_frac": nbytes / us / 1e3 / hbm,
+                        "tflop_s": flops / us / 1e6,
+                        "tensor_frac": flops / us / 1e6 / tc_peak})
+        del qw, x, y
     if args.profile:
         print(json.dumps({"profile": "micro", "filter": args.micro_filter}))
         return
@@ -773,12 +776,14 @@ def run_tp(args, wl):
     qkv = st.acts["qkv"]
     attn = st.acts["attn"]
 
+    dws = st.attn_ws.dec
+
     def attn_once():
-        L.call("ksh_decode_attention", qkv.data_ptr(), Bt, km.n_heads, km.n_kv_heads, d,
+        L.call("ksh_decode_attention_ws", qkv.data_ptr(), Bt, km.n_heads, km.n_kv_heads, d,
                st.positions.data_ptr(), st.slots.data_ptr(), rc.data_ptr(), rs.data_ptr(),
                rc.shape[0], pool.data_ptr(), nb_, L_, 0, bs_, st.block_tables.data_ptr(),
-               st.block_tables.shape[1], st.capacity, attn.data_ptr(), km.flags.data_ptr(),
-               L.stream_ptr())
+               st.block_tables.shape[1], st.capacity, attn.data_ptr(), dws.data_ptr(),
+               dws.numel(), km.flags.data_ptr(), L.stream_ptr())
     for _ in range(3):
         attn_once()
     r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -834,7 +839,7 @@ def run_tp(args, wl):
         e2e={"value": Bt / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": Bt * 8,
              "d2h_bytes_per_step": Bt * 8},
         roofline=roofline_entry(
-            "fused decode attention (ksh_decode_attention), one layer",
+            "fused decode attention (ksh_decode_attention_ws), one layer",
             attn_bytes, attn_ms, hbm, peak_kind,
             profiled_traffic("decode_attention_llama8b_b64_ctx4096") if ws == 1 else None,
             "profiles/decode_attention_llama8b_b64_ctx4096.md (ncu, one launch, TP1)"),
@@ -1191,6 +1196,48 @@ def run_profile_lm_head(args, wl):
                       "algorithmic_bytes": cfg.vocab * cfg.hidden * 4 + cfg.hidden * 8}))
 
 
+def run_profile_lm_head_tc(args, wl):
+    """The batch lm_head alone for an ncu capture: the workload's vocabulary x
+    hidden weight split into fp16 hi / lo (2.1 GB for the 8B shape; the fp32
+    copy is freed after the split) and one ksh_lm_head_argmax_tc call at 64
+    rows (fused final norm + tensor-core GEMM + argmax) between
+    cudaProfilerStart/Stop, after a warm-up."""
+    from kshipra_b200 import _lib as L
+    from kshipra_b200.config import PRESETS
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = PRESETS[wl["preset"]]
+    V, H, M = cfg.vocab, cfg.hidden, 64
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = torch.randn((V, H), generator=g, device=dev) * 0.02
+    hi = torch.empty((V, H), dtype=torch.float16, device=dev)
+    lo = torch.empty_like(hi)
+    inv = torch.empty(V, device=dev)
+    s = L.stream_ptr()
+    L.call("ksh_lm_head_split_weight", w.data_ptr(), V, H, hi.data_ptr(), lo.data_ptr(),
+           inv.data_ptr(), None, s)
+    torch.cuda.synchronize()
+    del w
+    nw = torch.ones(H, device=dev)
+    x = torch.randn((M, H), generator=g, device=dev)
+    tok = torch.empty(M, dtype=torch.int64, device=dev)
+    ws = torch.empty(int(L.lib().ksh_lm_head_tc_workspace_size(M, H, V)), dtype=torch.uint8,
+                     device=dev)
+
+    def run():
+        L.call("ksh_lm_head_argmax_tc", x.data_ptr(), M, H, nw.data_ptr(), 1e-6, hi.data_ptr(),
+               lo.data_ptr(), inv.data_ptr(), V, None, tok.data_ptr(), ws.data_ptr(), ws.numel(), s)
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStart()
+    run()
+    torch.cuda.synchronize()
+    torch.cuda.cudart().cudaProfilerStop()
+    print(json.dumps({"profile": "lm_head_tc", "workload": args.workload, "rows": M,
+                      "algorithmic_bytes": V * H * 4 + V * 4 + M * H * 4}))
+
+
 def run_profile_decode_attention(args, wl):
     """The tensor-parallel workload's roofline kernel alone, for an ncu
     capture: one layer's block pool for ``batch`` sequences at ``context``
@@ -1329,7 +1376,8 @@ def main():
                     help="run one request inside cudaProfilerStart/Stop (for ncu)")
     ap.add_argument("--trace", action="store_true",
                     help="with --profile: CUPTI trace of one request, per-kernel summary")
-    ap.add_argument("--profile-kernel", default=None, choices=["lm_head", "decode_attention"],
+    ap.add_argument("--profile-kernel", default=None,
+                    choices=["lm_head", "lm_head_tc", "decode_attention"],
                     help="with --profile: only this kernel on the workload's shape (small ncu case)")
     ap.add_argument("--micro-filter", default=None,
                     help="micro workload: comma list of scheme:M:KxN points to run")
@@ -1340,6 +1388,9 @@ def main():
     wl = WORKLOADS[args.workload]
     if args.profile and args.profile_kernel == "lm_head":
         run_profile_lm_head(args, wl)
+        return
+    if args.profile and args.profile_kernel == "lm_head_tc":
+        run_profile_lm_head_tc(args, wl)
         return
     if args.profile and args.profile_kernel == "decode_attention":
         run_profile_decode_attention(args, wl)

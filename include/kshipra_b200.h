@@ -81,6 +81,11 @@ int ksh_set_gemm_mid(int enabled);
  * previous setting.  A tuning switch with no counterpart in the reference;
  * results agree across splits within fp32 rounding. */
 int ksh_set_decode_split(int clusters);
+/* The same for ksh_decode_attention_ws: CTAs per (sequence, kv head) of the
+ * cluster-free key split, 1..8 (1 runs the unsplit kernel); 0 restores the
+ * per-launch choice.  KSH_DECODE_GSPLIT=1..8 in the environment sets it at
+ * load.  Returns the previous setting.  No counterpart in the reference. */
+int ksh_set_decode_gsplit(int splits);
 /* Kernels this library has launched since it was loaded, counting those
  * recorded into a CUDA graph under capture (a replay of that graph launches
  * them again without counting). */
@@ -210,6 +215,24 @@ int ksh_decode_attention(const float* qkv, int64_t batch, int64_t hq, int64_t hk
                          float* pool, int64_t num_blocks, int64_t num_layers, int64_t layer,
                          int64_t block_size, const int32_t* block_tables, int64_t max_blocks,
                          int64_t max_total_len, float* out, int32_t* flags, void* stream);
+
+/* The same fused decode step with a workspace for key-split partial
+ * states: the keys of each (sequence, kv head) are split over independent
+ * CTAs (1..8, chosen per launch so that the CTAs fill the SMs' resident
+ * slots) whose online-softmax states the last one to finish merges in split
+ * order; without the workspace the split is a thread-block cluster.  The
+ * workspace, of ksh_decode_attention_workspace_size(batch, hq, hkv, d) bytes
+ * and 256-byte aligned, must be zero before its first use; every launch
+ * leaves its counters at zero again, so a CUDA graph can replay the call
+ * without a memset in between. */
+int64_t ksh_decode_attention_workspace_size(int64_t batch, int64_t hq, int64_t hkv, int64_t d);
+int ksh_decode_attention_ws(const float* qkv, int64_t batch, int64_t hq, int64_t hkv, int64_t d,
+                            const int64_t* positions, const int64_t* slot_mapping,
+                            const float* rope_cos, const float* rope_sin, int64_t max_pos,
+                            float* pool, int64_t num_blocks, int64_t num_layers, int64_t layer,
+                            int64_t block_size, const int32_t* block_tables, int64_t max_blocks,
+                            int64_t max_total_len, float* out, void* workspace,
+                            int64_t workspace_bytes, int32_t* flags, void* stream);
 
 /* ------------------------------------------------------------------------
  * lm_head (fp32, never quantized; engine/model.py:151) fused with the greedy

@@ -53,6 +53,10 @@ SIGNATURES = {
                                   I64, I64, P, P, I64, P, P]),
     "ksh_decode_attention": (I32, [P, I64, I64, I64, I64, P, P, P, P, I64, P, I64, I64, I64,
                                    I64, P, I64, I64, P, P, P]),
+    "ksh_decode_attention_workspace_size": (I64, [I64, I64, I64, I64]),
+    "ksh_decode_attention_ws": (I32, [P, I64, I64, I64, I64, P, P, P, P, I64, P, I64, I64, I64,
+                                      I64, P, I64, I64, P, P, I64, P, P]),
+    "ksh_set_decode_gsplit": (I32, [I32]),
     "ksh_lm_head_workspace_size": (I64, [I64, I64]),
     "ksh_lm_head_argmax": (I32, [P, I64, I64, P, F32, P, I64, P, P, P, I64, P]),
     "ksh_lm_head_argmax_noalloc_max_bytes": (I64, []),

@@ -22,15 +22,24 @@ from ._lib import call, ptr, stream_ptr
 
 
 class AttentionWorkspace:
-    """Grow-only, zero-initialised split-K scratch (counters must start at 0)."""
+    """Grow-only split-K scratch: one buffer for the prefill attention (its
+    entry point clears its counters per call) and one for the fused decode
+    attention's key-split states (zeroed here once; its kernels leave the
+    counters at zero)."""
 
     def __init__(self):
         self.buf: Optional[torch.Tensor] = None
+        self.dec: Optional[torch.Tensor] = None
 
     def get(self, nbytes: int, device) -> torch.Tensor:
         if self.buf is None or self.buf.numel() < nbytes or self.buf.device != device:
             self.buf = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
         return self.buf
+
+    def decode(self, nbytes: int, device) -> torch.Tensor:
+        if self.dec is None or self.dec.numel() < nbytes or self.dec.device != device:
+            self.dec = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        return self.dec
 
 
 _WS = AttentionWorkspace()

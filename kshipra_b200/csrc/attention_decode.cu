@@ -67,6 +67,8 @@ struct DecArgs {
   const int32_t* block_tables;
   float* out;                // [B, hq, d]
   int32_t* flags;
+  float* gpart;              // key split without a cluster: [items][splits][G][D + 4] partial states
+  uint32_t* gcount;          // [items] CTAs finished per item (zero between launches)
   int64_t max_pos, num_blocks, num_layers, layer, hkv, hq, bs, max_blocks;
   int g;
   float scale;
@@ -110,7 +112,12 @@ struct DecLayout {
   static_assert(BAR_OFF % 2 == 0 && Q_OFF % 4 == 0 && P_OFF % 4 == 0, "alignment");
 };
 
-template <int D, int G>
+// GS: the key split runs over independent CTAs (gridDim.x of them per item)
+// instead of a cluster; each CTA leaves its state in a.gpart and the last of
+// an item to finish (a.gcount) merges them in split order and writes the
+// output.  Any split count then fills the SMs' resident slots, which a
+// cluster split, tied to cluster placement, does not.
+template <int D, int G, bool GS>
 __global__ void __launch_bounds__(kThreads, 2)
 decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
   using Ly = DecLayout<D, G>;
@@ -131,7 +138,8 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
   __shared__ int fail_s;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const uint32_t rank = cluster_rank(), csize = cluster_size();
+  const uint32_t rank = GS ? blockIdx.x : cluster_rank();
+  const uint32_t csize = GS ? gridDim.x : cluster_size();
   const int item = blockIdx.y;                  // (b, hk)
   const int b = item / static_cast<int>(a.hkv);
   const int hk = item - b * static_cast<int>(a.hkv);
@@ -409,9 +417,10 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
   }
   __syncthreads();
   float* part = ring + Ly::WST_F;                 // [kMaxCluster][G][D + 4] on rank 0
-  if (csize > 1) cluster_sync();                  // every rank is done with its ring
+  if (!GS && csize > 1) cluster_sync();           // every rank is done with its ring
   const uint32_t slot0 = smem_u32(part + static_cast<int>(rank) * G * (D + 4));
-  const uint32_t dst = csize > 1 ? map_rank(slot0, 0u) : slot0;
+  const uint32_t dst = (!GS && csize > 1) ? map_rank(slot0, 0u) : slot0;
+  float* gdst = GS ? a.gpart + (static_cast<int64_t>(item) * csize + rank) * G * (D + 4) : nullptr;
   for (int w = tid; w < G * D4; w += kThreads) {
     const int h = w / D4, c = w - h * D4;
     float M = -INFINITY;
@@ -431,27 +440,58 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
       A.z = fmaf(ar.z, wgt, A.z);
       A.w = fmaf(ar.w, wgt, A.w);
     }
-    st_cluster_f32x4(dst + static_cast<uint32_t>((h * (D + 4) + 4 + 4 * c) * 4), A);
-    if (c == 0) {
-      st_cluster_f32(dst + static_cast<uint32_t>(h * (D + 4) * 4), M);
-      st_cluster_f32(dst + static_cast<uint32_t>((h * (D + 4) + 1) * 4), Lsum);
+    if (GS) {
+      reinterpret_cast<float4*>(gdst + h * (D + 4) + 4)[c] = A;
+      if (c == 0) {
+        gdst[h * (D + 4)] = M;
+        gdst[h * (D + 4) + 1] = Lsum;
+      }
+    } else {
+      st_cluster_f32x4(dst + static_cast<uint32_t>((h * (D + 4) + 4 + 4 * c) * 4), A);
+      if (c == 0) {
+        st_cluster_f32(dst + static_cast<uint32_t>(h * (D + 4) * 4), M);
+        st_cluster_f32(dst + static_cast<uint32_t>((h * (D + 4) + 1) * 4), Lsum);
+      }
     }
   }
-  if (csize > 1) cluster_sync();                  // all ranks' states have landed in rank 0
-  else __syncthreads();
-  if (rank != 0) return;
+  const float* src_part = part;
+  if (GS) {
+    // the last CTA of the item to finish merges every split's state
+    __shared__ int last_s;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last_s = atomicAdd(a.gcount + item, 1u) == csize - 1u;
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+    src_part = a.gpart + static_cast<int64_t>(item) * csize * G * (D + 4);
+  } else {
+    if (csize > 1) cluster_sync();                // all ranks' states have landed in rank 0
+    else __syncthreads();
+    if (rank != 0) return;
+  }
+  // the states: in global memory (GS, written by other CTAs: read past L1)
+  // or in this CTA's shared memory (cluster rank 0)
+  auto ld1 = [](const float* q) -> float {
+    if constexpr (GS) return __ldcg(q);
+    else return *q;
+  };
+  auto ld4 = [](const float4* q) -> float4 {
+    if constexpr (GS) return __ldcg(q);
+    else return *q;
+  };
   for (int w = tid; w < G * D4; w += kThreads) {
     const int h = w / D4, c = w - h * D4;
     float M = -INFINITY;
-    for (uint32_t r = 0; r < csize; ++r) M = fmaxf(M, part[(r * G + h) * (D + 4)]);
+    for (uint32_t r = 0; r < csize; ++r) M = fmaxf(M, ld1(src_part + (r * G + h) * (D + 4)));
     const float Ms = isinf(M) ? 0.0f : M;
     float L = 0.0f;
     float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
     for (uint32_t r = 0; r < csize; ++r) {
-      const float* pr_ = part + (r * G + h) * (D + 4);
-      const float wgt = expf(pr_[0] - Ms);
-      L = fmaf(pr_[1], wgt, L);
-      const float4 ar = reinterpret_cast<const float4*>(pr_ + 4)[c];
+      const float* pr_ = src_part + (r * G + h) * (D + 4);
+      const float wgt = expf(ld1(pr_) - Ms);
+      L = fmaf(ld1(pr_ + 1), wgt, L);
+      const float4 ar = ld4(reinterpret_cast<const float4*>(pr_ + 4) + c);
       A.x = fmaf(ar.x, wgt, A.x);
       A.y = fmaf(ar.y, wgt, A.y);
       A.z = fmaf(ar.z, wgt, A.z);
@@ -464,6 +504,7 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
     o.w = __fdiv_rn(A.w, L);
     reinterpret_cast<float4*>(a.out + (static_cast<int64_t>(b) * a.hq + hk * G + h) * D)[c] = o;
   }
+  if (GS && tid == 0) a.gcount[item] = 0u;       // ready for the next launch
 }
 
 // Cluster size (key split) for a launch: the estimated time of
@@ -505,14 +546,50 @@ int choose_split(K kern, size_t smem, int64_t items, int64_t tiles, int* residen
   return best;
 }
 
+// Key split over independent CTAs (with a workspace for the partial
+// states): the estimated time of ceil(CTAs / resident CTAs) waves of (tiles
+// per CTA + 4 tiles for the prologue, the ramp and the merge), minimised
+// over 1..8, the smaller split on ties.
+int choose_gsplit(int resident_ctas, int64_t items, int64_t tiles) {
+  int best = 1;
+  double best_cost = 0.0;
+  const int64_t slots = static_cast<int64_t>(resident_ctas) * num_sms();
+  const int smax = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(kMaxCluster, tiles / 2)));
+  for (int sp = 1; sp <= smax; ++sp) {
+    const int64_t waves = (items * sp + slots - 1) / slots;
+    const double cost = static_cast<double>(waves) * (static_cast<double>((tiles + sp - 1) / sp) + 4.0);
+    if (sp == 1 || cost < best_cost) {
+      best = sp;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+// 0: split chosen per launch; KSH_DECODE_GSPLIT=1..8 forces the workspace path's split
+int g_forced_gsplit = [] {
+  const char* v = getenv("KSH_DECODE_GSPLIT");
+  const int c = (v && *v) ? atoi(v) : 0;
+  return c >= 1 && c <= 8 ? c : 0;
+}();
+
 template <int D, int G>
 int launch_dec(const CUtensorMap& map, const DecArgs& a, int64_t B, int64_t max_total_len,
                cudaStream_t stream) {
   using Ly = DecLayout<D, G>;
-  auto kern = decode_attn_kernel<D, G>;
-  if (set_smem_optin(reinterpret_cast<const void*>(kern), Ly::SMEM) != KSH_OK) return KSH_ERR_CUDA;
   const int64_t items = B * a.hkv;
   const int64_t tiles = (max_total_len + kTK - 1) / kTK;
+  if (a.gpart && items <= 65535) {
+    auto gkern = decode_attn_kernel<D, G, true>;
+    if (set_smem_optin(reinterpret_cast<const void*>(gkern), Ly::SMEM) != KSH_OK) return KSH_ERR_CUDA;
+    const int per_sm = resident_ctas(reinterpret_cast<const void*>(gkern), kThreads, Ly::SMEM);
+    const int sp = g_forced_gsplit > 0 ? g_forced_gsplit : choose_gsplit(per_sm, items, tiles);
+    if (sp > 1)
+      return launch(gkern, dim3(static_cast<unsigned>(sp), static_cast<unsigned>(items)),
+                    dim3(kThreads), Ly::SMEM, stream, map, a);
+  }
+  auto kern = decode_attn_kernel<D, G, false>;
+  if (set_smem_optin(reinterpret_cast<const void*>(kern), Ly::SMEM) != KSH_OK) return KSH_ERR_CUDA;
   static int resident[kMaxCluster + 1] = {};     // resident clusters per cluster size
   const int cluster = g_forced_split > 0 ? g_forced_split
                                          : choose_split(kern, Ly::SMEM, items, tiles, resident);
@@ -540,6 +617,46 @@ int launch_dec(const CUtensorMap& map, const DecArgs& a, int64_t B, int64_t max_
 
 using namespace ksh;
 
+namespace {
+constexpr int kGMaxSplit = kMaxCluster;
+
+int64_t dec_counter_bytes(int64_t items) { return (items * 4 + 255) / 256 * 256; }
+
+int decode_attention_impl(const float* qkv, int64_t batch, int64_t hq, int64_t hkv, int64_t d,
+                          const int64_t* positions, const int64_t* slot_mapping,
+                          const float* rope_cos, const float* rope_sin, int64_t max_pos,
+                          float* pool, int64_t num_blocks, int64_t num_layers, int64_t layer,
+                          int64_t block_size, const int32_t* block_tables, int64_t max_blocks,
+                          int64_t max_total_len, float* out, void* workspace,
+                          int64_t workspace_bytes, int32_t* flags, void* stream);
+}  // namespace
+
+extern "C" int64_t ksh_decode_attention_workspace_size(int64_t batch, int64_t hq, int64_t hkv,
+                                                       int64_t d) {
+  if (batch <= 0 || hq <= 0 || hkv <= 0 || hq % hkv != 0 || d <= 0) return 0;
+  const int64_t items = batch * hkv;
+  return dec_counter_bytes(items) + items * kGMaxSplit * (hq / hkv) * (d + 4) * 4;
+}
+
+extern "C" int ksh_decode_attention_ws(const float* qkv, int64_t batch, int64_t hq, int64_t hkv,
+                                       int64_t d, const int64_t* positions,
+                                       const int64_t* slot_mapping, const float* rope_cos,
+                                       const float* rope_sin, int64_t max_pos, float* pool,
+                                       int64_t num_blocks, int64_t num_layers, int64_t layer,
+                                       int64_t block_size, const int32_t* block_tables,
+                                       int64_t max_blocks, int64_t max_total_len, float* out,
+                                       void* workspace, int64_t workspace_bytes, int32_t* flags,
+                                       void* stream) {
+  KSH_CHECK_ARG(workspace != nullptr);
+  if (workspace_bytes < ksh_decode_attention_workspace_size(batch, hq, hkv, d))
+    return KSH_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return KSH_ERR_ALIGN;
+  return decode_attention_impl(qkv, batch, hq, hkv, d, positions, slot_mapping, rope_cos, rope_sin,
+                               max_pos, pool, num_blocks, num_layers, layer, block_size,
+                               block_tables, max_blocks, max_total_len, out, workspace,
+                               workspace_bytes, flags, stream);
+}
+
 extern "C" int ksh_decode_attention(const float* qkv, int64_t batch, int64_t hq, int64_t hkv,
                                     int64_t d, const int64_t* positions,
                                     const int64_t* slot_mapping, const float* rope_cos,
@@ -548,6 +665,21 @@ extern "C" int ksh_decode_attention(const float* qkv, int64_t batch, int64_t hq,
                                     int64_t block_size, const int32_t* block_tables,
                                     int64_t max_blocks, int64_t max_total_len, float* out,
                                     int32_t* flags, void* stream) {
+  return decode_attention_impl(qkv, batch, hq, hkv, d, positions, slot_mapping, rope_cos, rope_sin,
+                               max_pos, pool, num_blocks, num_layers, layer, block_size,
+                               block_tables, max_blocks, max_total_len, out, nullptr, 0, flags,
+                               stream);
+}
+
+namespace {
+int decode_attention_impl(const float* qkv, int64_t batch, int64_t hq, int64_t hkv, int64_t d,
+                          const int64_t* positions, const int64_t* slot_mapping,
+                          const float* rope_cos, const float* rope_sin, int64_t max_pos,
+                          float* pool, int64_t num_blocks, int64_t num_layers, int64_t layer,
+                          int64_t block_size, const int32_t* block_tables, int64_t max_blocks,
+                          int64_t max_total_len, float* out, void* workspace,
+                          int64_t workspace_bytes, int32_t* flags, void* stream) {
+  (void)workspace_bytes;
   KSH_CHECK_ARG(batch > 0 && hq > 0 && hkv > 0 && hq % hkv == 0 && max_pos > 0);
   KSH_CHECK_ARG(num_blocks > 0 && num_layers > 0 && layer >= 0 && layer < num_layers);
   KSH_CHECK_ARG(max_blocks > 0 && max_total_len > 0 && batch * hkv <= 65535);
@@ -577,6 +709,10 @@ extern "C" int ksh_decode_attention(const float* qkv, int64_t batch, int64_t hq,
   a.max_blocks = max_blocks;
   a.g = static_cast<int>(g);
   a.scale = static_cast<float>(1.0 / sqrt(static_cast<double>(d)));
+  if (workspace) {
+    a.gcount = static_cast<uint32_t*>(workspace);
+    a.gpart = reinterpret_cast<float*>(static_cast<char*>(workspace) + dec_counter_bytes(batch * hkv));
+  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   // the pool as a 2-D tensor of token rows (D floats each) for TMA
   const int64_t rows = num_blocks * num_layers * 2 * hkv * block_size;
@@ -593,9 +729,16 @@ extern "C" int ksh_decode_attention(const float* qkv, int64_t batch, int64_t hq,
 #undef KSH_DEC
   return KSH_ERR_UNSUPPORTED;
 }
+}  // namespace
 
 extern "C" int ksh_set_decode_split(int clusters) {
   const int prev = g_forced_split;
   g_forced_split = clusters >= 1 && clusters <= kMaxCluster ? clusters : 0;
+  return prev;
+}
+
+extern "C" int ksh_set_decode_gsplit(int splits) {
+  const int prev = g_forced_gsplit;
+  g_forced_gsplit = splits >= 1 && splits <= kGMaxSplit ? splits : 0;
   return prev;
 }

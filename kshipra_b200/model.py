@@ -303,14 +303,17 @@ class KshipraModel:
         # fused RoPE + K/V write + attention kernel
         fused = (max_q_len == 1 and T == num_seqs and self.fused_decode and bs % 16 == 0
                  and d in (64, 128) and self.n_heads // self.n_kv_heads in _DECODE_GROUPS[d])
+        if fused:   # key-split partial states (zeroed once; the kernels leave the counters at 0)
+            dec_ws = attn_ws.decode(int(_lib.lib().ksh_decode_attention_workspace_size(
+                T, self.n_heads, self.n_kv_heads, d)), self.device)
         for i, Ly in enumerate(self.layers):
             linear_launch(hid, Ly.qkv.qw, Ly.qkv.w, Ly.qkv.bias, qkv, ws=lin_ws, norm_w=Ly.ln1,
                           eps=eps)
             if fused:
-                call("ksh_decode_attention", ptr(qkv), T, self.n_heads, self.n_kv_heads, d,
+                call("ksh_decode_attention_ws", ptr(qkv), T, self.n_heads, self.n_kv_heads, d,
                      ptr(positions), ptr(slots), ptr(rc), ptr(rs), rc.shape[0], ptr(pool), nb, L,
                      i, bs, ptr(block_tables), block_tables.shape[1], max_total_len, ptr(attn),
-                     ptr(self.flags), s)
+                     ptr(dec_ws), dec_ws.numel(), ptr(self.flags), s)
             else:
                 call("ksh_rope_kv_write", ptr(qkv), T, self.n_heads, self.n_kv_heads,
                      self.head_dim, ptr(positions), ptr(slots), ptr(rc), ptr(rs), rc.shape[0],
@@ -631,6 +634,8 @@ class DecodeState:
         nbytes = int(_lib.lib().ksh_paged_attention_workspace_size(
             B, model.n_heads, model.n_kv_heads, model.head_dim, 1, self.capacity))
         self.attn_ws.get(nbytes, dev)
+        self.attn_ws.decode(int(_lib.lib().ksh_decode_attention_workspace_size(
+            B, model.n_heads, model.n_kv_heads, model.head_dim)), dev)
         self.lm_ws = torch.empty(model.lm_ws_bytes(B), dtype=torch.uint8, device=dev)
         if B > LM_GEMV_ROWS and model.lm_tc:
             model.lm_head_split()        # before any graph capture of the step

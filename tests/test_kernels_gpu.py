@@ -751,6 +751,29 @@ def test_fused_decode_attention_long_context_batch64():
             _lib.lib().ksh_set_decode_split(prev)
         assert int(flags.item()) == 0, (split, int(flags.item()))
         outs[split] = out
+    # the workspace entry point: the cluster-free key split at the per-launch
+    # choice and forced to 2..8 CTAs, each launch twice on one workspace (the
+    # counters it leaves must serve the next launch)
+    wsz = int(_lib.lib().ksh_decode_attention_workspace_size(B, hq, hkv, D))
+    dws = torch.zeros(wsz, dtype=torch.uint8, device=dev)
+    for gsplit in (0, 2, 3, 4, 5, 8):
+        out = torch.empty((B, hq, D), device=dev)
+        flags = torch.zeros(1, dtype=torch.int32, device=dev)
+        prev = _lib.lib().ksh_set_decode_gsplit(gsplit)
+        try:
+            for _ in range(2):
+                _lib.call("ksh_decode_attention_ws", qkv.data_ptr(), B, hq, hkv, D,
+                          pos.data_ptr(), slots.data_ptr(), rc.data_ptr(), rs.data_ptr(),
+                          rc.shape[0], pool.data_ptr(), nb, 1, 0, bs, bt.data_ptr(), maxb,
+                          ctx + 1, out.data_ptr(), dws.data_ptr(), wsz, flags.data_ptr(),
+                          _lib.stream_ptr())
+            torch.cuda.synchronize()
+        finally:
+            _lib.lib().ksh_set_decode_gsplit(prev)
+        assert int(flags.item()) == 0, (gsplit, int(flags.item()))
+        outs[f"ws{gsplit}"] = out
+    wsz_counters = (B * hkv * 4 + 255) // 256 * 256
+    assert int(dws[:wsz_counters].sum()) == 0          # counters left at zero
     half = D // 2
     for b in (0, 9, 33, 63):
         p = int(positions[b])
