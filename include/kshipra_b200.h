@@ -75,6 +75,14 @@ int ksh_set_gemv_dp4a(int enabled);
  * setting.  A tuning switch with no counterpart in the reference; results
  * agree with the prefill GEMM within fp32 rounding. */
 int ksh_set_gemm_mid(int enabled);
+/* Rows of x from which the prefill GEMM first widens the whole quantized
+ * weight to fp16 in the workspace (one pass, exact) and then streams fp16
+ * tiles by TMA straight into the MMA (default 512; 0 never;
+ * KSH_GEMM_PREDEQ_MIN in the environment sets it at load).  Below it each
+ * output tile widens its own weight tiles.  ksh_linear_workspace_size counts
+ * the fp16 copy for such m.  Returns the previous setting.  A tuning switch
+ * with no counterpart in the reference; results are identical either way. */
+int64_t ksh_set_gemm_predeq(int64_t min_rows);
 /* Key split of ksh_decode_attention: the number of CTAs (one thread-block
  * cluster) that share a (sequence, kv head), 1..8; 0 or out of range restores
  * the per-launch choice (waves of resident CTAs x keys per CTA).  Returns the

@@ -33,6 +33,7 @@ SIGNATURES = {
     "ksh_set_gemv_tc": (I32, [I32]),
     "ksh_set_gemv_dp4a": (I32, [I32]),
     "ksh_set_gemm_mid": (I32, [I32]),
+    "ksh_set_gemm_predeq": (I64, [I64]),
     "ksh_set_decode_split": (I32, [I32]),
     "ksh_kernel_launches": (ctypes.c_uint64, []),
     "ksh_pack_int8": (I32, [P, I64, I64, P, P, P, P]),

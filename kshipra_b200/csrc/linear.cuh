@@ -68,6 +68,8 @@ int set_gemv_tc_mode(int mode);
 int set_gemv_resident_enabled(int on);
 bool gemv_resident_enabled();
 int launch_gemm_simt(int wk, int epi, const LinArgs& a, cudaStream_t stream);
+// Rows from which the prefill GEMM widens the weight to fp16 once per call (0: never).
+int64_t set_gemm_predeq_min(int64_t rows);
 // One-row INT4 linear with dp4a integer dot products (gemv_i4_dp4a.cu).
 bool gemv_i4_dp4a_eligible(int wk, int epi, const LinArgs& a);
 int launch_gemv_i4_dp4a(int epi, const LinArgs& a, cudaStream_t stream);

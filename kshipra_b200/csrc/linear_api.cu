@@ -266,3 +266,4 @@ extern "C" int ksh_lm_head_argmax(const float* x, int64_t m, int64_t hidden,
 
 extern "C" int ksh_set_gemv_dp4a(int enabled) { return set_gemv_dp4a_mode(enabled); }
 extern "C" int ksh_set_gemm_mid(int enabled) { return set_gemm_mid_mode(enabled); }
+extern "C" int64_t ksh_set_gemm_predeq(int64_t min_rows) { return set_gemm_predeq_min(min_rows); }

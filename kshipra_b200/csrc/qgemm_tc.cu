@@ -20,6 +20,11 @@
 //   warps 2-5: dequantize the raw weight tile to fp16 in the UMMA K-major
 //             128B-swizzled layout, then the epilogue (tcgen05.ld -> scales ->
 //             bias / residual / SwiGLU -> global)
+// For M >= kPreMinRows (a prefill chunk of many token tiles) the weight tile
+// would be dequantized once per token tile; instead a pass before the GEMM
+// widens the whole weight to fp16 q (exact, unscaled) in the workspace and the
+// GEMM (PRE) loads fp16 tiles by TMA straight into the MMA's B operand: warps
+// 2-5 only apply the scales (INT4 group promotion) and run the epilogue.
 // Split-K over CTAs writes fp32 partial tiles to the workspace; the last CTA
 // of a tile sums them in split order (deterministic) and runs the epilogue.
 // Every mbarrier wait is bounded; a timeout raises KSH_FLAG_TIMEOUT in the
@@ -52,6 +57,11 @@ constexpr int RING_BYTES = NS * STAGE_BYTES + NB * BH_BYTES;
 constexpr int OUT_LD = BN + 4;             // staging tile row stride (floats)
 static_assert(BM * OUT_LD * 4 <= NS * STAGE_BYTES, "output staging reuses the TMA ring");
 constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(RING_BYTES) + 2 * BN * 4 + BN * 4 + 512;
+// PRE: a stage holds x hi, x lo and the fp16 weight tile
+constexpr int PRE_STAGE_BYTES = 2 * A_BYTES + BH_BYTES;
+constexpr int PRE_RING_BYTES = NS * PRE_STAGE_BYTES;
+static_assert(BM * OUT_LD * 4 <= PRE_RING_BYTES, "output staging reuses the PRE ring");
+constexpr size_t PRE_SMEM_BYTES = 1024 + static_cast<size_t>(PRE_RING_BYTES) + 2 * BN * 4 + BN * 4 + 512;
 
 struct TcArgs {
   const __half* scales;
@@ -87,14 +97,16 @@ __device__ __forceinline__ uint32_t i4x2_to_h2(uint32_t w, int nib0) {
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-template <int WK, int EPI>
+template <int WK, int EPI, bool PRE>
 __global__ void __launch_bounds__(kThreads, 1)
 qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constant__ CUtensorMap map_xl,
                 const __grid_constant__ CUtensorMap map_w, TcArgs a) {
+  constexpr int SB = PRE ? PRE_STAGE_BYTES : STAGE_BYTES;
+  constexpr int RB = PRE ? PRE_RING_BYTES : RING_BYTES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* bh_base = smem + NS * STAGE_BYTES;
-  float* sc_s = reinterpret_cast<float*>(smem + RING_BYTES);     // [2][BN] weight scales per group
+  uint8_t* bh_base = smem + NS * SB;
+  float* sc_s = reinterpret_cast<float*>(smem + RB);             // [2][BN] weight scales per group
   float* bias_s = sc_s + 2 * BN;                                  // [BN]
   uint64_t* bars = reinterpret_cast<uint64_t*>(bias_s + BN);
   uint64_t* full = bars;                       // [NS]  TMA landed
@@ -116,9 +128,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
   const int ktpg = WK == WK_I4 ? a.kt_per_group : max(ntl, 1);
   const int ngl = (ntl + ktpg - 1) / ktpg;
 
-  auto stage_ah = [&](int s) { return smem + s * STAGE_BYTES; };
-  auto stage_al = [&](int s) { return smem + s * STAGE_BYTES + A_BYTES; };
-  auto stage_br = [&](int s) { return smem + s * STAGE_BYTES + 2 * A_BYTES; };
+  auto stage_ah = [&](int s) { return smem + s * SB; };
+  auto stage_al = [&](int s) { return smem + s * SB + A_BYTES; };
+  auto stage_br = [&](int s) { return smem + s * SB + 2 * A_BYTES; };   // raw or (PRE) fp16 tile
   auto tile_bh = [&](int b) { return bh_base + b * BH_BYTES; };
 
   if (threadIdx.x == 0) {
@@ -154,7 +166,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
 
   if (warp == 0) {
     if (lane == 0) {
-      const uint32_t bytes = 2 * A_BYTES + (WK == WK_I8 ? BN * BK : BN * BK / 2);
+      const uint32_t bytes = 2 * A_BYTES + (PRE ? BH_BYTES : (WK == WK_I8 ? BN * BK : BN * BK / 2));
       for (int i = 0; i < ntl && !*abort_flag; ++i) {
         const int s = i % NS;
         if (i >= NS && !mbar_wait(&empty[s], ((i / NS) - 1) & 1)) {
@@ -165,9 +177,9 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
         const int kg = (kt_begin + i) * BK;
         tma_load_2d(stage_ah(s), &map_xh, &full[s], kg, m0);
         tma_load_2d(stage_al(s), &map_xl, &full[s], kg, m0);
-        const int xw = WK == WK_I8 ? kg : kg / 2;
+        const int xw = (PRE || WK == WK_I8) ? kg : kg / 2;
         if (EPI == EPI_SWIGLU) {
-          const int half_bytes = (WK == WK_I8 ? BK : BK / 2) * (BN / 2);
+          const int half_bytes = (PRE ? 2 * BK : (WK == WK_I8 ? BK : BK / 2)) * (BN / 2);
           tma_load_2d(stage_br(s), &map_w, &full[s], xw, n_tile * (BN / 2));
           tma_load_2d(stage_br(s) + half_bytes, &map_w, &full[s], xw, a.inter + n_tile * (BN / 2));
         } else {
@@ -186,13 +198,15 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
           *abort_flag = 1;
           break;
         }
-        if (!mbar_wait(&bready[b], (i / NB) & 1)) {      // implies full[s] completed
+        // PRE: the fp16 tile came with the stage; else the converters' barrier
+        // implies full[s] completed
+        if (!mbar_wait(PRE ? &full[s] : &bready[b], PRE ? (i / NS) & 1 : (i / NB) & 1)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
         const uint32_t ah = smem_u32(stage_ah(s)), al = smem_u32(stage_al(s)),
-                       bh = smem_u32(tile_bh(b));
+                       bh = smem_u32(PRE ? stage_br(s) : tile_bh(b));
         const uint32_t d = tmem + buf * BN;
 #pragma unroll
         for (int kk = 0; kk < BK / 16; ++kk) {
@@ -201,7 +215,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
           mma_f16(d, desc_k_sw128(al + kk * 32), bd, idesc, 1u);
         }
         mma_commit(&empty[s]);
-        mma_commit(&bfree[b]);
+        if (!PRE) mma_commit(&bfree[b]);
         if ((i % ktpg) == ktpg - 1 || i == ntl - 1) mma_commit(&acc_full[buf]);
       }
     }
@@ -245,8 +259,28 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
       return true;
     };
 
+    auto group_scale = [&](int gl) {       // scale of row t for group gl, into slot gl & 1
+      float scv = 0.0f;
+      if (wrow_t >= 0) {
+        if (WK == WK_I8) scv = __half2float(a.scales[wrow_t]);
+        else scv = __half2float(a.scales[static_cast<int64_t>(wrow_t) * a.ngroups_row +
+                                         (kt_begin + gl * ktpg) / ktpg]);
+      }
+      sc_s[(gl & 1) * BN + t] = scv;
+    };
     bool ok = true;
-    for (int i = 0; i < ntl && ok; ++i) {
+    if (PRE) {
+      // the weight tiles need no conversion: scales and promotion only
+      for (int gl = 0; gl < ngl && ok; ++gl) {
+        if (*abort_flag) {
+          ok = false;
+          break;
+        }
+        group_scale(gl);
+        if (gl >= 1 && !promote(gl - 1)) ok = false;
+      }
+    }
+    for (int i = 0; i < (PRE ? 0 : ntl) && ok; ++i) {
       const int s = i % NS, b = i % NB;
       const int gl = i / ktpg;
       if (*abort_flag || !mbar_wait(&full[s], (i / NS) & 1)) {
@@ -257,15 +291,7 @@ qgemm_tc_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constan
         ok = false;
         break;
       }
-      if ((i % ktpg) == 0) {                 // group scale of row t, into slot gl & 1
-        float scv = 0.0f;
-        if (wrow_t >= 0) {
-          if (WK == WK_I8) scv = __half2float(a.scales[wrow_t]);
-          else scv = __half2float(a.scales[static_cast<int64_t>(wrow_t) * a.ngroups_row +
-                                           (kt_begin + gl * ktpg) / ktpg]);
-        }
-        sc_s[(gl & 1) * BN + t] = scv;
-      }
+      if ((i % ktpg) == 0) group_scale(gl);
       // dequantize row t of the raw tile (TMA-swizzled) into the 128B-swizzled fp16 tile
       uint8_t* dst_row = tile_bh(b) + (t >> 3) * 1024 + (t & 7) * 128;
       const uint32_t rsw = static_cast<uint32_t>(t & 7);
@@ -600,20 +626,66 @@ int max_splits(int64_t m, int64_t n) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, kMaxSplits)));
 }
 
+// Rows of x from which the prefill GEMM widens the weight once per call
+// (KSH_GEMM_PREDEQ_MIN in the environment sets it; 0 turns it off).
+int64_t g_pre_min = [] {
+  const char* v = getenv("KSH_GEMM_PREDEQ_MIN");
+  return (v && *v) ? static_cast<int64_t>(atoll(v)) : static_cast<int64_t>(512);
+}();
+
+bool use_pre(int64_t m) { return g_pre_min > 0 && m >= g_pre_min; }
+
 struct WsLayout {
-  int64_t xh, xl, inv, total;
+  int64_t xh, xl, inv, wq, total;
 };
 
-// Workspace: the fp16 hi / lo split of x and the per-row factors.  (Split-K
-// partial sums never leave the SMs: they are reduced over the cluster.)
+// Workspace: the fp16 hi / lo split of x and the per-row factors, and for
+// the PRE path the fp16 copy of the weight (rows x K rounded up to a group of
+// 128).  (Split-K partial sums never leave the SMs: they are reduced over the
+// cluster.)
 WsLayout ws_layout(int64_t m, int64_t k, int64_t n_rows) {
-  (void)n_rows;
   WsLayout w = {};
   w.xh = 0;
   w.xl = w.xh + align256(m * k * 2);
   w.inv = w.xl + align256(m * k * 2);
-  w.total = w.inv + align256(m * 4);
+  w.wq = w.inv + align256(m * 4);
+  w.total = w.wq + (use_pre(m) && n_rows > 0 ? align256(n_rows * ((k + 127) / 128 * 128) * 2) : 0);
   return w;
+}
+
+// Packed weight -> fp16 q (exact, unscaled), row-major [rows, keff]; one
+// 16-byte payload chunk per thread (INT8: 16 values, INT4: 32, low nibble =
+// even k).
+template <int WK>
+__global__ void __launch_bounds__(256)
+dequant_w_kernel(const uint8_t* __restrict__ w, int64_t rows, int64_t row_bytes, int64_t keff,
+                 __half* __restrict__ out) {
+  grid_dep_wait();
+  grid_dep_launch();
+  const int64_t chunks_row = row_bytes / 16;
+  const int64_t total = rows * chunks_row;
+  for (int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; c < total;
+       c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = c / chunks_row, j = c - r * chunks_row;
+    const uint4 v = *reinterpret_cast<const uint4*>(w + r * row_bytes + j * 16);
+    const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
+    __half* dst = out + r * keff + j * (WK == WK_I8 ? 16 : 32);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      uint4 o;
+      if (WK == WK_I8) {
+        o.x = i8x2_to_h2(ws[e], 0);
+        o.y = i8x2_to_h2(ws[e], 2);
+        reinterpret_cast<uint2*>(dst)[e] = make_uint2(o.x, o.y);
+      } else {
+        o.x = i4x2_to_h2(ws[e], 0);
+        o.y = i4x2_to_h2(ws[e], 2);
+        o.z = i4x2_to_h2(ws[e], 4);
+        o.w = i4x2_to_h2(ws[e], 6);
+        reinterpret_cast<uint4*>(dst)[e] = o;
+      }
+    }
+  }
 }
 
 struct TcPlan {
@@ -654,13 +726,31 @@ int launch_tc(const LinArgs& a, char* ws, cudaStream_t stream) {
                 CU_TENSOR_MAP_SWIZZLE_128B))
     return KSH_ERR_CUDA;
   const uint32_t box_rows = EPI == EPI_SWIGLU ? BN / 2 : BN;
-  // raw weight tiles: 64-byte (int8) / 32-byte (int4) rows, TMA-swizzled so the
-  // dequantizing threads read them without bank conflicts
-  const bool ok = WK == WK_I8
-                      ? make_tensor_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.k, n_rows, a.k, BK,
-                                 box_rows, CU_TENSOR_MAP_SWIZZLE_64B)
-                      : make_tensor_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.kp / 2, n_rows,
-                                 a.kp / 2, BK / 2, box_rows, CU_TENSOR_MAP_SWIZZLE_32B);
+  // the workspace's fp16 weight region holds rows x (K rounded up to 128)
+  const bool pre = use_pre(a.m) && keff <= (a.k + 127) / 128 * 128;
+  bool ok;
+  if (pre) {
+    // widen the whole weight once to fp16 q; the GEMM loads 128-byte rows of
+    // it (128B swizzle, the MMA's K-major operand layout) straight by TMA
+    __half* wq = reinterpret_cast<__half*>(ws + L.wq);
+    const int64_t row_bytes = WK == WK_I8 ? a.k : a.kp / 2;
+    const int64_t chunks = n_rows * (row_bytes / 16);
+    const int64_t blocks = std::min<int64_t>((chunks + 255) / 256, static_cast<int64_t>(num_sms()) * 8);
+    st = launch(WK == WK_I8 ? dequant_w_kernel<WK_I8> : dequant_w_kernel<WK_I4>,
+                dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
+                static_cast<const uint8_t*>(a.w), n_rows, row_bytes, keff, wq);
+    if (st != KSH_OK) return st;
+    ok = make_tensor_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, wq, keff, n_rows, keff * 2, BK,
+                            box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    // raw weight tiles: 64-byte (int8) / 32-byte (int4) rows, TMA-swizzled so
+    // the dequantizing threads read them without bank conflicts
+    ok = WK == WK_I8
+             ? make_tensor_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.k, n_rows, a.k, BK,
+                                  box_rows, CU_TENSOR_MAP_SWIZZLE_64B)
+             : make_tensor_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT8, a.w, a.kp / 2, n_rows,
+                                  a.kp / 2, BK / 2, box_rows, CU_TENSOR_MAP_SWIZZLE_32B);
+  }
   if (!ok) return KSH_ERR_CUDA;
   TcArgs t = {};
   t.scales = a.scales;
@@ -677,14 +767,15 @@ int launch_tc(const LinArgs& a, char* ws, cudaStream_t stream) {
   t.kt_per_group = p.kt_per_group;
   t.ngroups_row = WK == WK_I4 ? static_cast<int>(a.kp / a.g) : 1;
   t.g = static_cast<int>(a.g);
-  auto kern = qgemm_tc_kernel<WK, EPI>;
-  if (set_smem_optin(reinterpret_cast<const void*>(kern), SMEM_BYTES) != KSH_OK) return KSH_ERR_CUDA;
+  auto kern = pre ? qgemm_tc_kernel<WK, EPI, true> : qgemm_tc_kernel<WK, EPI, false>;
+  const size_t smem_bytes = pre ? PRE_SMEM_BYTES : SMEM_BYTES;
+  if (set_smem_optin(reinterpret_cast<const void*>(kern), smem_bytes) != KSH_OK) return KSH_ERR_CUDA;
   const unsigned gx = EPI == EPI_SWIGLU ? static_cast<unsigned>((a.inter + BN / 2 - 1) / (BN / 2))
                                         : static_cast<unsigned>(p.tiles_n);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(gx, static_cast<unsigned>(p.tiles_m), static_cast<unsigned>(p.splits));
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;      // the splits of a tile = one cluster
@@ -712,6 +803,12 @@ int launch_split_x(const LinArgs& a, char* ws, bool perm, __half** xh, __half** 
 }
 
 int64_t split_x_workspace_size(int64_t m, int64_t k) { return ws_layout(m, k, 0).total; }
+
+int64_t set_gemm_predeq_min(int64_t rows) {
+  const int64_t prev = g_pre_min;
+  g_pre_min = rows > 0 ? rows : 0;
+  return prev;
+}
 
 int64_t gemm_tc_workspace_size(int64_t m, int64_t k, int64_t n) {
   if (m <= 16) return 0;

@@ -935,3 +935,74 @@ def test_model_lm_head_paths_agree():
     scale = float(lg_f.abs().max())
     assert float((lg_tc - lg_f).abs().max()) <= 1e-5 * scale
     assert tok_tc.tolist() == tok_f.tolist()
+
+
+@pytest.mark.parametrize("scheme", ["int4", "int8"])
+@pytest.mark.parametrize("m", [1, 8, 40, 130])
+def test_linear_with_outlier_features(scheme, m):
+    """Activation rows with a few outlier features, 1e3 to 1e4 times the rest
+    of their row (as real checkpoints have), through every quantized-linear
+    path: one row (INT4 dp4a GEMV / INT8 tensor-core GEMV), 8 rows (tensor-core
+    decode kernel), 40 rows (batched-decode kernel), 130 rows (prefill GEMM).
+    The activations are carried as 22-bit fixed point per 32-element vector
+    (dp4a) or per row (hi + lo fp16), so the features next to an outlier keep
+    fewer bits; the bound is the one the other linear tests use, per row
+    against float64 with the dequantized weight: max |error| <= 2e-5 x
+    max |y|, with the fp32 reference's own error printed beside it."""
+    from kshipra_b200.quantization import (linear_launch, quantize_int4_per_group,
+                                           quantize_int8_per_channel)
+    gen = torch.Generator().manual_seed(77 + m)
+    K, N = 4096, 512
+    x = torch.randn((m, K), generator=gen)
+    for r in range(m):
+        idx = torch.randint(0, K, (4,), generator=gen)
+        x[r, idx] *= torch.tensor([1e3, -3e3, 6e3, 1e4])
+    w = torch.randn((N, K), generator=gen) * 0.03
+    if scheme == "int8":
+        qw = quantize_int8_per_channel(w.cuda())
+        wd = oq.dequantize_int8(*oq.quantize_int8_per_channel(w.numpy()))
+    else:
+        qw = quantize_int4_per_group(w.cuda(), 128)
+        p, s, _ = oq.quantize_int4_per_group(w.numpy(), 128)
+        wd = oq.dequantize_int4(p, s, K, 128)
+    y64 = x.double().numpy() @ wd.astype(np.float64).T
+    y32 = (x @ torch.from_numpy(wd.astype(np.float32)).T).double().numpy()   # fp32 F.linear
+    y = torch.empty((m, N), device="cuda")
+    linear_launch(x.cuda(), qw, None, None, y)
+    den = np.abs(y64).max(axis=1)
+    err = np.abs(y.cpu().numpy() - y64).max(axis=1) / den
+    err32 = np.abs(y32 - y64).max(axis=1) / den
+    assert err.max() <= 2e-5, (scheme, m, float(err.max()), float(err32.max()))
+
+
+@pytest.mark.parametrize("scheme,g", [("int8", 0), ("int4", 128), ("int4", 64)])
+@pytest.mark.parametrize("m,k,n", [(600, 1000, 640), (2048, 4096, 768), (512, 896, 1216)])
+def test_prefill_gemm_widened_weight_path_matches(scheme, g, m, k, n):
+    """The prefill GEMM with the weight widened to fp16 once per call (PRE)
+    and with per-tile widening give the same output, bit for bit (the same
+    MMAs in the same order), for the store and SwiGLU epilogues, with bias
+    and residual, and K not a multiple of the 128-wide group."""
+    from kshipra_b200 import _lib
+    from kshipra_b200.quantization import (linear_launch, quantize_int4_per_group,
+                                           quantize_int8_per_channel, swiglu_launch)
+    gen = torch.Generator().manual_seed(m + k + n + g)
+    x = torch.randn((m, k), generator=gen).cuda()
+    w = (torch.randn((n, k), generator=gen) * 0.02).cuda()
+    b = torch.randn((n,), generator=gen).cuda()
+    res = torch.randn((m, n), generator=gen).cuda()
+    qw = quantize_int8_per_channel(w) if scheme == "int8" else quantize_int4_per_group(w, g)
+    outs = []
+    prev = _lib.lib().ksh_set_gemm_predeq(512)
+    try:
+        for mode in (512, 0):
+            _lib.lib().ksh_set_gemm_predeq(mode)
+            y = res.clone()
+            linear_launch(x, qw, None, b, y, residual=y)
+            h = torch.empty((m, n // 2), device="cuda")
+            swiglu_launch(x, qw, None, n // 2, h)
+            torch.cuda.synchronize()
+            outs.append((y.cpu(), h.cpu()))
+    finally:
+        _lib.lib().ksh_set_gemm_predeq(prev)
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert torch.equal(outs[0][1], outs[1][1])
