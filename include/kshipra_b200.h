@@ -305,6 +305,28 @@ int ksh_decode_advance(const int64_t* next, int64_t batch, int64_t* ids,
                        int64_t* step, int32_t* flags, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Sum all-reduce of the tensor-parallel partial sums over peer memory (one
+ * process per GPU; the reference is single-process and has none: this
+ * replaces the collective after the row-parallel o_proj / down_proj of this
+ * build's sharded KshipraModel.forward, engine/model.py:111-148).
+ * peer_buffers: device array of `world` pointers, every rank's buffer of
+ * ksh_peer_allreduce_buffer_floats(n_max, world) floats mapped into this
+ * process (symmetric memory), zeroed before the first call.  A call sums the
+ * n floats (n % 4 == 0, n <= n_max) each rank left at float offset
+ * parity * n_max of its buffer into out (reduce-scatter + all-gather over
+ * plain peer loads; each slice summed once in rank order, so every rank
+ * gets the same bits).  Consecutive calls must alternate parity 0 / 1 and
+ * come in the same order on every rank.  epochs: ksh_peer_allreduce_epoch_words()
+ * zeroed words of device memory per rank.  Waits for peers are bounded
+ * (KSH_FLAG_TIMEOUT in *flags).
+ * ---------------------------------------------------------------------- */
+int64_t ksh_peer_allreduce_buffer_floats(int64_t n_max, int world);
+int64_t ksh_peer_allreduce_epoch_words(void);
+int ksh_peer_allreduce_f32(const uint64_t* peer_buffers, int rank, int world, int64_t n,
+                           int64_t n_max, int parity, float* out, uint32_t* epochs,
+                           int32_t* flags, void* stream);
+
+/* ------------------------------------------------------------------------
  * Failure-path check of the device waits (no counterpart in the reference;
  * it stands in for the reference's timeout-and-report handling of a stuck
  * worker, benchmarks/run_benchmarks.py:234-267, at the device level).  One

@@ -65,6 +65,9 @@ SIGNATURES = {
     "ksh_argmax_rows": (I32, [P, I64, I64, P, P]),
     "ksh_decode_advance": (I32, [P, I64, P, P, P, P, P, I64, I64, P, I64, P, P, P]),
     "ksh_check_bounded_wait": (I32, [I64, I32, P, P, P, P]),
+    "ksh_peer_allreduce_buffer_floats": (I64, [I64, I32]),
+    "ksh_peer_allreduce_epoch_words": (I64, []),
+    "ksh_peer_allreduce_f32": (I32, [P, I32, I32, I64, I64, I32, P, P, P, P]),
     "ksh_lm_head_tc_workspace_size": (I64, [I64, I64, I64]),
     "ksh_lm_head_split_weight": (I32, [P, I64, I64, P, P, P, P, P]),
     "ksh_lm_head_argmax_tc": (I32, [P, I64, I64, P, F32, P, P, P, I64, P, P, P, I64, P]),

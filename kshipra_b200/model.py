@@ -28,6 +28,7 @@ into those buffers.
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Sequence
 
@@ -48,6 +49,7 @@ FLAG_NAMES = {1: "non-finite weight", 2: "block id out of range", 4: "slot out o
               32: "sequence longer than its block table", 64: "a bounded device wait gave up"}
 FLAG_TIMEOUT = 64
 LM_GEMV_ROWS = 16            # lm_head rows served by the fp32 GEMV; more go to tensor cores
+PEER_AR_ROWS = 256           # token rows of a row-parallel sum done over peer memory
 
 
 # GQA group sizes the fused decode-attention kernel is instantiated for, per head dim.
@@ -149,6 +151,13 @@ class KshipraModel:
         self.fused_decode = True
         with torch.cuda.device(self.device):
             self._load(state_dict)
+        # Row-parallel sums of up to PEER_AR_ROWS rows over peer memory (a
+        # collective set-up: every rank builds its shard at the same point);
+        # KSH_PEER_AR=0 in the environment keeps NCCL for them.
+        self._peer_ar = None
+        if self.tp_world > 1 and os.environ.get("KSH_PEER_AR", "1") != "0":
+            from .peer_allreduce import PeerAllReduce
+            self._peer_ar = PeerAllReduce(self.tp_group, self.device, PEER_AR_ROWS * self.hidden)
 
     # ------------------------------------------------------------------ #
     # weights
@@ -320,20 +329,32 @@ class KshipraModel:
                      ptr(q), ptr(pool), nb, L, i, bs, ptr(self.flags), s)
                 paged_attention(q, pool, i, block_tables, q_start, prefix_lens, max_q_len,
                                 max_total_len, attn, self.flags, ws=attn_ws)
-            # row-parallel o / down: rank 0 adds the residual, the others write
-            # their partial sums, and the all-reduce completes hidden on every rank
-            res = hid if self.tp_rank == 0 else None
-            linear_launch(attn.view(T, -1), Ly.o.qw, Ly.o.w, None, hid, residual=res, ws=lin_ws)
-            self._all_reduce(hid)
+            self._row_parallel(attn.view(T, -1), Ly.o, hid, lin_ws)
             swiglu_launch(hid, Ly.gate_up.qw, Ly.gate_up.w, self.inter, h, ws=lin_ws,
                           norm_w=Ly.ln2, eps=eps)
-            linear_launch(h, Ly.down.qw, Ly.down.w, None, hid, residual=res, ws=lin_ws)
-            self._all_reduce(hid)
+            self._row_parallel(h, Ly.down, hid, lin_ws)
         return hid
 
-    def _all_reduce(self, t: torch.Tensor) -> None:
-        if self.tp_world > 1:
-            torch.distributed.all_reduce(t, group=self.tp_group)
+    def _row_parallel(self, x_in: torch.Tensor, proj: "_Proj", hid: torch.Tensor,
+                      lin_ws: Workspace) -> None:
+        """hid += x_in @ W^T, W split by input columns over the ranks: rank 0
+        adds the residual, every rank its partial sum, then the sum over the
+        ranks.  Up to the peer buffer's size the partial goes straight into
+        symmetric memory and this library's peer all-reduce sums it; larger
+        ones (prefill chunks) use NCCL."""
+        if self.tp_world == 1:
+            linear_launch(x_in, proj.qw, proj.w, None, hid, residual=hid, ws=lin_ws)
+            return
+        res = hid if self.tp_rank == 0 else None
+        n = hid.numel()
+        par = self._peer_ar
+        if par is not None and n <= par.n_max and n % 4 == 0:
+            dst = par.partial(n).view(hid.shape)
+            linear_launch(x_in, proj.qw, proj.w, None, dst, residual=res, ws=lin_ws)
+            par.reduce(hid, n)
+        else:
+            linear_launch(x_in, proj.qw, proj.w, None, hid, residual=res, ws=lin_ws)
+            torch.distributed.all_reduce(hid, group=self.tp_group)
 
     def lm_ws_bytes(self, m: int) -> int:
         """Workspace bytes of the lm_head call for ``m`` rows."""

@@ -124,3 +124,75 @@ def test_tensor_parallel_two_gpus_matches_single_gpu():
     for name, (toks, ref, err) in out.items():
         assert toks == ref, (name, toks, ref)
         assert err < 1e-3, (name, err)
+
+
+def _ar_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import datetime
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    try:
+        from kshipra_b200.peer_allreduce import PeerAllReduce
+        par = PeerAllReduce(None, dev, 64 * 4096)
+        res = []
+        # consecutive eager calls (alternating buffers), then the same calls
+        # captured in a CUDA graph and replayed
+        sizes = [64 * 4096, 4096, 20 * 4096, 64 * 4096, 8, 64 * 4096]
+        for i, n in enumerate(sizes):
+            g = torch.Generator(device=dev).manual_seed(100 * i + rank)
+            part = torch.randn(n, generator=g, device=dev)
+            par.partial(n).copy_(part)
+            y = torch.empty(n, device=dev)
+            par.reduce(y, n)
+            full = torch.empty((world, n), device=dev)
+            dist.all_gather_into_tensor(full, part)
+            ref = full.double().sum(0)
+            ys = torch.empty((world, n), device=dev)
+            dist.all_gather_into_tensor(ys, y)
+            err = float((y.double() - ref).abs().max() / ref.abs().max())
+            res.append((err, bool(torch.equal(ys[0], ys[-1]))))
+        n = 64 * 4096
+        src = [torch.randn(n, generator=torch.Generator(device=dev).manual_seed(7 + 10 * k + rank),
+                           device=dev) for k in range(2)]
+        outs = [torch.empty(n, device=dev) for _ in range(2)]
+        graph = torch.cuda.CUDAGraph()
+        s_ = torch.cuda.Stream(device=dev)
+        s_.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s_):
+            with torch.cuda.graph(graph, stream=s_):
+                for k in range(2):
+                    par.partial(n).copy_(src[k])
+                    par.reduce(outs[k], n)
+        torch.cuda.current_stream().wait_stream(s_)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        for k in range(2):
+            full = torch.empty((world, n), device=dev)
+            dist.all_gather_into_tensor(full, src[k])
+            ref = full.double().sum(0)
+            res.append((float((outs[k].double() - ref).abs().max() / ref.abs().max()), True))
+        res.append((float(par.flags.item()), True))
+        del graph
+        torch.cuda.synchronize()
+        dist.barrier()
+        if rank == 0:
+            out["ar"] = res
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_allreduce_two_gpus():
+    """The peer-memory all-reduce of the row-parallel partial sums: the
+    float64 sum to fp32 rounding, identical bits on every rank, across
+    consecutive calls of different sizes and in CUDA-graph replays, with no
+    bounded wait giving up."""
+    out = mp.get_context("spawn").Manager().dict()
+    mp.spawn(_ar_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    res = out["ar"]
+    for err, same in res[:-1]:
+        assert err < 1e-6 and same, res
+    assert res[-1][0] == 0.0, res
