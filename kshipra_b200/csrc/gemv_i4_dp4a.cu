@@ -9,7 +9,8 @@
 //   below 2^21) and X = rint(x * 2^E) is stored as three balanced signed
 //   8-bit digits, X = d0 + 256 d1 + 65536 d2, in shared memory -- once per
 //   CTA, in the byte order of the unpacked weights (elements 0,2,4,6 then
-//   1,3,5,7 of every 8);
+//   1,3,5,7 of every 8), one 112-byte record per vector (the digits, 8 sum X
+//   and 2^-E) so a vector costs seven conflict-free 16-byte shared loads;
 // * a weight word of 8 nibbles becomes two words of q + 8 (0..15) with one or
 //   two logic operations, and dp4a multiplies them with the digits: per
 //   vector sum (q + 8) X = sum_p 256^p sum (q + 8) d_p in int32, minus the
@@ -18,9 +19,10 @@
 //   group scale times 2^-E in fp32;
 // * each warp owns two weight rows (gate and up for SwiGLU), so one load of
 //   the digits serves both; lanes stride over the row's 16-byte vectors with
-//   four vectors per row in flight, and each warp keeps an L2 bulk prefetch
-//   of its next rows (weights and group scales) running; a row pair's scales
-//   are staged in the warp's shared memory before its vectors are read.
+//   four vectors per row in flight (the remainder one at a time, no per-vector
+//   bounds tests in the main loop), and each warp keeps an L2 bulk prefetch of
+//   its next rows (weights and group scales) running; group scales are read
+//   through the read-only cache.
 //
 // Against the CUDA-core fp32 GEMV (a byte permute, a float add and an FMA per
 // weight, fp32 x re-read per row) this is about 1.5 instructions per weight,
@@ -40,6 +42,7 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kUnroll = 4;      // 16-byte vectors per lane and row in flight
 constexpr int kPfItems = 4;     // row items a warp keeps prefetched ahead
+constexpr int kRec = 7;         // 16-byte words per vector record (6 digit words + meta)
 
 __device__ __forceinline__ int dp4a(uint32_t a, uint32_t b, int c) {
   return __dp4a(static_cast<int>(a), static_cast<int>(b), c);
@@ -86,11 +89,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 gemv_i4_dp4a_kernel(LinArgs a, int64_t items_per_cta) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int nv = static_cast<int>(a.kp / 32);
-  uint4* dig = reinterpret_cast<uint4*>(smem);             // [3 planes][2 halves][nv]
-  int* cor = reinterpret_cast<int*>(smem + 96 * static_cast<size_t>(nv));   // [nv] 8 sum X
-  float* sv = reinterpret_cast<float*>(cor + nv);           // [nv] 2^-E
-  const int ngi = static_cast<int>(a.kp / a.g);
-  __half* sw = reinterpret_cast<__half*>(sv + nv) + (threadIdx.x >> 5) * 2 * ngi;   // this warp's [2][ng]
+  // per 32-element vector one 112-byte record: the three digit planes (two
+  // 16-byte halves each), then {8 sum X, 2^-E bits, 0, 0}; 28 words apart, so
+  // the lanes of a quarter warp read their records from distinct banks
+  uint4* rec = reinterpret_cast<uint4*>(smem);              // [nv][kRec]
   __shared__ float red[kWarps];
   __shared__ float inv_s;
 
@@ -201,7 +203,7 @@ gemv_i4_dp4a_kernel(LinArgs a, int64_t items_per_cta) {
     sumx += __shfl_xor_sync(0xffffffffu, sumx, 1);
     sumx += __shfl_xor_sync(0xffffffffu, sumx, 2);
     if (act) {
-      uint32_t* dw = reinterpret_cast<uint32_t*>(dig);
+      uint32_t* rw = reinterpret_cast<uint32_t*>(rec + static_cast<size_t>(v) * kRec);
 #pragma unroll
       for (int p = 0; p < 3; ++p) {
         // byte p of each y, elements (0,2,4,6) and (1,3,5,7)
@@ -211,13 +213,13 @@ gemv_i4_dp4a_kernel(LinArgs a, int64_t items_per_cta) {
         const uint32_t even = __byte_perm(e02, e46, 0x5410) ^ 0x80808080u;
         const uint32_t odd = __byte_perm(e13, e57, 0x5410) ^ 0x80808080u;
         // words 2q, 2q + 1 of plane p: half q / 2, words (2q) % 4 and + 1
-        uint32_t* h = dw + ((p * 2 + (q >> 1)) * nv + v) * 4 + 2 * (q & 1);
+        uint32_t* h = rw + (p * 2 + (q >> 1)) * 4 + 2 * (q & 1);
         h[0] = even;
         h[1] = odd;
       }
       if (q == 0) {
-        cor[v] = 8 * sumx;
-        sv[v] = ldexpf(1.0f, -E);
+        rw[24] = static_cast<uint32_t>(8 * sumx);
+        rw[25] = __float_as_uint(ldexpf(1.0f, -E));
       }
     }
   }
@@ -235,47 +237,39 @@ gemv_i4_dp4a_kernel(LinArgs a, int64_t items_per_cta) {
     }
     int64_t r0, r1;
     rows_of(it, r0, r1);
-    const char* w0 = W + r0 * rb;
-    const char* w1 = W + (r1 >= 0 ? r1 : r0) * rb;
-    {
-      const __half* s0 = a.scales + r0 * ng;
-      const __half* s1 = a.scales + (r1 >= 0 ? r1 : r0) * ng;
-      __syncwarp();                               // the previous item's reads are done
-      for (int t = lane; t < ngi; t += 32) {
-        sw[t] = s0[t];
-        sw[ngi + t] = s1[t];
-      }
-      __syncwarp();
-    }
+    const uint4* w0 = reinterpret_cast<const uint4*>(W + r0 * rb);
+    const uint4* w1 = reinterpret_cast<const uint4*>(W + (r1 >= 0 ? r1 : r0) * rb);
+    const __half* s0 = a.scales + r0 * ng;
+    const __half* s1 = a.scales + (r1 >= 0 ? r1 : r0) * ng;
     float acc0 = 0.0f, acc1 = 0.0f;
-    for (int v0 = lane; v0 < nv; v0 += 32 * kUnroll) {
+    // one vector: its digit record is shared by the two rows
+    auto vec = [&](int v, const uint4& wa, const uint4& wb) {
+      const uint4* rc = rec + static_cast<size_t>(v) * kRec;
+      uint4 d[6];
+#pragma unroll
+      for (int h = 0; h < 6; ++h) d[h] = rc[h];
+      const uint4 meta = rc[6];
+      const uint32_t e0 = static_cast<uint32_t>(v) * 32u;
+      const uint32_t grp = g_pow2 ? (e0 >> g_shift) : e0 / g;
+      const float e = __uint_as_float(meta.y);
+      const int c = static_cast<int>(meta.x);
+      const int t0 = vec_dot(wa, d) - c;
+      const int t1 = vec_dot(wb, d) - c;
+      acc0 = fmaf(__int2float_rn(t0), __half2float(__ldg(s0 + grp)) * e, acc0);
+      acc1 = fmaf(__int2float_rn(t1), __half2float(__ldg(s1 + grp)) * e, acc1);
+    };
+    int v0 = lane;
+    for (; v0 + 32 * (kUnroll - 1) < nv; v0 += 32 * kUnroll) {
       uint4 wa[kUnroll], wb[kUnroll];
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
-        const int v = v0 + 32 * u;
-        if (v < nv) {
-          wa[u] = ld_stream(w0 + static_cast<int64_t>(v) * 16);
-          wb[u] = ld_stream(w1 + static_cast<int64_t>(v) * 16);
-        }
+        wa[u] = ld_stream(w0 + v0 + 32 * u);
+        wb[u] = ld_stream(w1 + v0 + 32 * u);
       }
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int v = v0 + 32 * u;
-        if (v < nv) {
-          uint4 d[6];
-#pragma unroll
-          for (int h = 0; h < 6; ++h) d[h] = dig[h * nv + v];
-          const int c = cor[v];
-          const float e = sv[v];
-          const uint32_t e0 = static_cast<uint32_t>(v) * 32u;
-          const int64_t grp = g_pow2 ? (e0 >> g_shift) : e0 / g;
-          const int t0 = vec_dot(wa[u], d) - c;
-          const int t1 = vec_dot(wb[u], d) - c;
-          acc0 = fmaf(__int2float_rn(t0), __half2float(sw[grp]) * e, acc0);
-          acc1 = fmaf(__int2float_rn(t1), __half2float(sw[ngi + grp]) * e, acc1);
-        }
-      }
+      for (int u = 0; u < kUnroll; ++u) vec(v0 + 32 * u, wa[u], wb[u]);
     }
+    for (; v0 < nv; v0 += 32) vec(v0, ld_stream(w0 + v0), ld_stream(w1 + v0));
     acc0 = warp_sum(acc0);
     acc1 = warp_sum(acc1);
     if (lane == 0) {
@@ -303,9 +297,7 @@ int g_dp4a_mode = [] {
   return (v && *v) ? (atoi(v) != 0 ? 1 : 0) : 1;
 }();
 
-size_t dp4a_smem(const LinArgs& a) {
-  return static_cast<size_t>(a.kp / 32) * 104 + static_cast<size_t>(kWarps) * 2 * (a.kp / a.g) * 2;
-}
+size_t dp4a_smem(const LinArgs& a) { return static_cast<size_t>(a.kp / 32) * kRec * 16; }
 
 }  // namespace
 
@@ -319,8 +311,7 @@ bool gemv_i4_dp4a_eligible(int wk, int epi, const LinArgs& a) {
   if (g_dp4a_mode == 0 || wk != WK_I4 || a.m != 1 || a.argmax_out) return false;
   if (a.g % 32 != 0 || a.kp % 32 != 0 || (reinterpret_cast<uintptr_t>(a.w) & 15) != 0) return false;
   if (epi == EPI_SWIGLU && !a.y) return false;
-  // the digits of x live in shared memory (104 bytes per 32 elements), and
-  // each warp's two rows of group scales
+  // the digits of x live in shared memory (112 bytes per 32 elements)
   return dp4a_smem(a) <= 100 * 1024;
 }
 
