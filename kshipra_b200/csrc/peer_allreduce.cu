@@ -40,7 +40,7 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kMaxRanks = 8;
-constexpr int kGrid = 32;                 // CTAs per call (every rank the same)
+constexpr int kGrid = 128;                // CTAs per call (every rank the same)
 constexpr uint32_t kSpin = 1u << 22;      // polls of a flag before giving up (~0.3 s)
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -81,7 +81,7 @@ __device__ bool barrier_peers(const ArArgs& a, int ph, uint32_t e, int64_t flag_
         arrived = true;
         break;
       }
-      __nanosleep(64);
+      if (it >= 256) __nanosleep(64);         // poll fast first: the peers are usually close
     }
     if (!arrived) ok_s = 0;
   }
@@ -106,31 +106,45 @@ peer_allreduce_kernel(ArArgs a) {
   const int64_t sub4 = (slice4 + kGrid - 1) / kGrid;
   bool ok = barrier_peers(a, 0, e, flag_off);
   if (ok) {
+    // every rank's float4 of this position loaded before any is added, so
+    // the peer round trips overlap; summed in rank order
     const int64_t lo = a.rank * slice4 + blockIdx.x * sub4;
     const int64_t hi = min(min(lo + sub4, (a.rank + 1) * slice4), n4);
     float4* red = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.peers[a.rank]) + r_off);
     for (int64_t i = lo + threadIdx.x; i < hi; i += kThreads) {
-      float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+      float4 v[kMaxRanks];
 #pragma unroll
-      for (int r = 0; r < kMaxRanks; ++r) {
+      for (int r = 0; r < kMaxRanks; ++r)
+        if (r < R)
+          v[r] = __ldcv(reinterpret_cast<const float4*>(
+                            reinterpret_cast<const float*>(a.peers[r]) + p_off) + i);
+      float4 s = v[0];
+#pragma unroll
+      for (int r = 1; r < kMaxRanks; ++r)
         if (r < R) {
-          const float4 v = __ldcv(reinterpret_cast<const float4*>(
-                                      reinterpret_cast<const float*>(a.peers[r]) + p_off) + i);
-          s.x += v.x; s.y += v.y; s.z += v.z; s.w += v.w;
+          s.x += v[r].x; s.y += v[r].y; s.z += v[r].z; s.w += v[r].w;
         }
-      }
       red[i] = s;
     }
     ok = barrier_peers(a, 1, e, flag_off);
   }
   if (ok) {
+    // sub-range c of every rank's slice: one float4 per rank in flight
     float4* out4 = reinterpret_cast<float4*>(a.out);
-    for (int r = 0; r < R; ++r) {
-      const int64_t lo = r * slice4 + blockIdx.x * sub4;
-      const int64_t hi = min(min(lo + sub4, (r + 1) * slice4), n4);
-      const float4* src = reinterpret_cast<const float4*>(
-                              reinterpret_cast<const float*>(a.peers[r]) + r_off);
-      for (int64_t i = lo + threadIdx.x; i < hi; i += kThreads) out4[i] = __ldcv(src + i);
+    for (int64_t j = threadIdx.x; j < sub4; j += kThreads) {
+      float4 v[kMaxRanks];
+#pragma unroll
+      for (int r = 0; r < kMaxRanks; ++r) {
+        const int64_t i = r * slice4 + blockIdx.x * sub4 + j;
+        if (r < R && blockIdx.x * sub4 + j < slice4 && i < n4)
+          v[r] = __ldcv(reinterpret_cast<const float4*>(
+                            reinterpret_cast<const float*>(a.peers[r]) + r_off) + i);
+      }
+#pragma unroll
+      for (int r = 0; r < kMaxRanks; ++r) {
+        const int64_t i = r * slice4 + blockIdx.x * sub4 + j;
+        if (r < R && blockIdx.x * sub4 + j < slice4 && i < n4) out4[i] = v[r];
+      }
     }
   } else if (threadIdx.x == 0) {
     raise_flag(a.flags, KSH_FLAG_TIMEOUT);
