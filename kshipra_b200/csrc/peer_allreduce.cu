@@ -22,6 +22,10 @@
 // 2. it announces that, waits for all peers, and gathers sub-range c of every
 //    rank's slice from the peers' reduced buffers into the output.
 //
+// With two ranks one phase does: after the first barrier every rank sums all
+// n floats from both partial buffers itself (the reads of the second phase
+// would cost as much as the extra reads, and a barrier more).
+//
 // Every rank gets the same bits (each slice is summed once, in rank order).
 // A CTA only waits for the CTAs of the same index on the other GPUs, so no
 // CTA of one GPU waits for another of the same GPU; the grid is small enough
@@ -41,6 +45,7 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kMaxRanks = 8;
 constexpr int kGrid = 128;                // CTAs per call (every rank the same)
+constexpr int kOneShotRanks = 2;          // up to this many ranks: one phase, every rank sums all
 constexpr uint32_t kSpin = 1u << 22;      // polls of a flag before giving up (~0.3 s)
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -69,7 +74,8 @@ __device__ bool barrier_peers(const ArArgs& a, int ph, uint32_t e, int64_t flag_
   __syncthreads();
   const int R = a.world;
   if (threadIdx.x < R) {
-    __threadfence_system();
+    // the release store at system scope orders this CTA's earlier writes
+    // (made visible to this thread by the barrier above) before the flag
     uint32_t* fl = reinterpret_cast<uint32_t*>(reinterpret_cast<float*>(a.peers[threadIdx.x]) + flag_off);
     st_release_sys(fl + (ph * kGrid + blockIdx.x) * R + a.rank, e);
     const uint32_t* mine = reinterpret_cast<const uint32_t*>(
@@ -105,6 +111,31 @@ peer_allreduce_kernel(ArArgs a) {
   const int64_t slice4 = (n4 + R - 1) / R;
   const int64_t sub4 = (slice4 + kGrid - 1) / kGrid;
   bool ok = barrier_peers(a, 0, e, flag_off);
+  if (ok && R <= kOneShotRanks) {
+    // one shot: this CTA's 1/G of all n floats straight from every rank's
+    // partial, summed in rank order -- one barrier, no second phase
+    const int64_t per = (n4 + kGrid - 1) / kGrid;
+    const int64_t lo = blockIdx.x * per, hi = min(lo + per, n4);
+    float4* out4 = reinterpret_cast<float4*>(a.out);
+    for (int64_t i = lo + threadIdx.x; i < hi; i += kThreads) {
+      float4 v[kOneShotRanks];
+#pragma unroll
+      for (int r = 0; r < kOneShotRanks; ++r)
+        if (r < R)
+          v[r] = __ldcv(reinterpret_cast<const float4*>(
+                            reinterpret_cast<const float*>(a.peers[r]) + p_off) + i);
+      float4 s = v[0];
+#pragma unroll
+      for (int r = 1; r < kOneShotRanks; ++r)
+        if (r < R) {
+          s.x += v[r].x; s.y += v[r].y; s.z += v[r].z; s.w += v[r].w;
+        }
+      out4[i] = s;
+    }
+    grid_dep_launch();
+    if (threadIdx.x == 0) a.epochs[blockIdx.x] = e;
+    return;
+  }
   if (ok) {
     // every rank's float4 of this position loaded before any is added, so
     // the peer round trips overlap; summed in rank order
