@@ -1242,8 +1242,8 @@ def run_profile_decode_attention(args, wl):
     """The tensor-parallel workload's roofline kernel alone, for an ncu
     capture: one layer's block pool for ``batch`` sequences at ``context``
     earlier positions (fp32 K/V, 2.2 GB for the 8B shape at TP1) and one
-    ksh_decode_attention call between cudaProfilerStart/Stop, after a
-    warm-up."""
+    ksh_decode_attention_ws call (the model's) between
+    cudaProfilerStart/Stop, after a warm-up."""
     from kshipra_b200 import _lib as L
     from kshipra_b200.config import PRESETS
     dev = torch.device("cuda", 0)
@@ -1262,13 +1262,15 @@ def run_profile_decode_attention(args, wl):
     rc, rs = torch.cos(ang.expand(-1, d // 2)).contiguous(), torch.sin(ang.expand(-1, d // 2)).contiguous()
     out = torch.empty((Bt, hq, d), device=dev)
     flags = torch.zeros(1, dtype=torch.int32, device=dev)
+    wsz = int(L.lib().ksh_decode_attention_workspace_size(Bt, hq, hkv, d))
+    dws = torch.zeros(wsz, dtype=torch.uint8, device=dev)
     s = L.stream_ptr()
 
     def run():
-        L.call("ksh_decode_attention", qkv.data_ptr(), Bt, hq, hkv, d, pos.data_ptr(),
+        L.call("ksh_decode_attention_ws", qkv.data_ptr(), Bt, hq, hkv, d, pos.data_ptr(),
                slots.data_ptr(), rc.data_ptr(), rs.data_ptr(), rc.shape[0], pool.data_ptr(),
                pool.shape[0], 1, 0, bs, bt.data_ptr(), nbs, ctx + 1, out.data_ptr(),
-               flags.data_ptr(), s)
+               dws.data_ptr(), wsz, flags.data_ptr(), s)
     for _ in range(3):
         run()
     torch.cuda.synchronize()
