@@ -103,6 +103,10 @@ int num_sms();
 int set_smem_optin(const void* kernel, size_t bytes);
 // CTAs of `kernel` resident per SM at this block size / dynamic smem (cached).
 int resident_ctas(const void* kernel, int threads, size_t smem);
+// CTAs of `kernel` resident on the GPU at once when launched in clusters of
+// `cluster` CTAs (cluster placement can leave SMs unusable; cached).  The
+// kernel's shared-memory opt-in must be set first.
+int64_t cluster_slots(const void* kernel, int threads, size_t smem, int cluster);
 
 }  // namespace ksh
 

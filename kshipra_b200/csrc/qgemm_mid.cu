@@ -9,22 +9,28 @@
 // * swap-AB: the MMA's M side (128 TMEM lanes) is 128 weight rows, its N side
 //   the MP = 32 or 64 token rows (zero-filled past m by TMA);
 // * x is split once per call (split_x_kernel: optional RMSNorm, a power-of-two
-//   row scale, x * 2^e = hi + lo in fp16); the lo tile sits right after the hi
-//   tile, so one MMA of N = 2 * MP takes both terms into separate TMEM columns
-//   (an M = 128 tcgen05.mma takes max(~45, N / 2) cycles, so the wider MMA
-//   costs little more than one of the two narrow ones);
+//   row scale, x * 2^e = hi + lo in fp16).  INT8: the lo tile sits right
+//   after the hi tile, so one MMA of N = 2 * MP takes both terms into
+//   separate TMEM columns (an M = 128 tcgen05.mma takes max(~45, N / 2)
+//   cycles); INT4: two MMAs of N = MP add both terms into the same columns,
+//   which leaves TMEM room for two accumulator buffers;
 // * raw int8 / int4 weight tiles arrive by TMA and converter warps widen them
-//   to fp16 (exact) in the 128B-swizzled K-major layout; INT4 chunks are
-//   widened in the order [0,2,4,6,1,3,5,7], and split_x stores x in the same
-//   order (a permutation of k applied to both operands leaves the sum as is);
+//   to fp16 (exact) straight into TMEM (tcgen05.st, one weight row per lane),
+//   where the MMAs take them as the A operand: only the x tiles are read from
+//   shared memory by the tensor core.  (With both operands in shared memory
+//   an N = 128 MMA alone reads 128 bytes per cycle, the whole shared-memory
+//   bandwidth, and the TMA and converter traffic came on top of it.)  INT4
+//   chunks are widened in the order [0,2,4,6,1,3,5,7], and split_x stores x
+//   in the same order (a permutation of k applied to both operands leaves
+//   the sum as is);
 // * a CTA covers NT = 2 tiles of 128 weight rows, so each x stage fetched from
-//   L2 feeds NT * 4 MMAs; each tile has its own MMA-issuing thread (one thread
-//   issues a tcgen05.mma only every ~70 cycles once commits are counted), and
-//   that thread waits once per stage, on the converters' barrier alone (an
-//   mbarrier wait stalls the issuing thread until its MMAs in flight finish);
+//   L2 feeds every tile's MMAs; one warp issues them all, converged, from
+//   one elected lane (an M = 128 tcgen05.mma with A in TMEM takes ~34 cycles
+//   at N = 64 and ~64 at N = 128; a lone lane-0 thread of a diverged warp
+//   issues one only every ~67 cycles), waiting once per stage;
 // * INT4 group scales are applied by promoting each group's TMEM partial into
-//   register accumulators (double-buffered TMEM, an add and an FMA per token
-//   and row); INT8 accumulates the whole K-slice in TMEM and scales once;
+//   register accumulators (double-buffered TMEM, an FMA per token and row);
+//   INT8 accumulates the whole K-slice in TMEM and scales once;
 // * split-K over a thread-block cluster, reduced through distributed shared
 //   memory in rank order (deterministic); the epilogue applies the row factor
 //   2^-e, bias, residual or SwiGLU (tile = 64 gate rows + the 64 matching up
@@ -56,35 +62,37 @@ using namespace tc;
 constexpr int BW = 128;                 // weight rows per tile (MMA M)
 constexpr int BK = 64;                  // K per stage (one 128-byte fp16 row)
 constexpr int NT = 2;                   // weight tiles per CTA
-constexpr int NA = 2;                   // fp16 weight operand buffers
-// warp 0: TMA; warp 1: MMAs of tile 0; warps 2 .. 1 + 4 NT: converters;
-// warps 2 + 4 NT ..: MMAs of tiles 1 .. NT - 1 (one issuing thread per tile:
-// a single thread issues a tcgen05.mma only every ~70 cycles, slower than the
-// tensor core runs these N = 64 / 128 MMAs)
+constexpr int NA = 4;                   // fp16 weight operand buffers (in TMEM)
+// warp 0: TMA; warp 1: MMAs of every tile (the whole warp converged, one
+// elected lane issuing); warps 2 .. 1 + 4 NT: converters
 constexpr int kConvWarp0 = 2;
-constexpr int kMmaWarpHi = kConvWarp0 + 4 * NT;
-constexpr int kThreads = 32 * (kMmaWarpHi + NT - 1);
+constexpr int kThreads = 32 * (kConvWarp0 + 4 * NT);
 constexpr int kMaxSplits = 8;
-constexpr int A_TILE = BW * BK * 2;     // 16 KB
 
 template <int WK, int MP>
 struct MidLayout {
   static constexpr int XT = MP * BK * 2;                      // one x term tile
   static constexpr int RAWT = BW * (WK == WK_I8 ? BK : BK / 2);
   static constexpr int STAGE = 2 * XT + NT * RAWT;
-  static constexpr int ABUF = NT * A_TILE;
-  static constexpr int NS = std::min(8, (200 * 1024 - NA * ABUF) / STAGE);
+  static constexpr int NS = std::min(8, (200 * 1024) / STAGE);
   static constexpr int RING = NS * STAGE;
-  static constexpr int A_OFF = RING;
-  static constexpr int BAR_OFF = A_OFF + NA * ABUF;
+  static constexpr int BAR_OFF = RING;
   static constexpr int BYTES = BAR_OFF + 512;
   static constexpr int OUT_LD = NT * BW;                      // staged partials [MP][NT * BW]
-  // per tile and buffer: [hi-term columns: MP][lo-term columns: MP]
-  static constexpr uint32_t TMEM_COLS = (WK == WK_I4 ? 2 : 1) * NT * 2 * MP;
-  static_assert(NS >= 3, "pipeline depth");
+  // TMEM columns.  Accumulators from column 0, per tile and buffer: INT4 MP
+  // columns (the hi- and lo-term MMAs add into the same ones), two buffers
+  // (one group promoted while the next accumulates); INT8 [hi: MP][lo: MP],
+  // one buffer.  From A_COL the fp16 weight operands: per buffer and tile
+  // BK / 2 columns (two K-consecutive halves per column, one row per lane).
+  static constexpr uint32_t ACC_COLS = WK == WK_I4 ? MP : 2 * MP;
+  static constexpr uint32_t A_COL = 256;
+  static constexpr uint32_t A_COLS = BK / 2;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(NS >= 4, "pipeline depth");
   static_assert(MP * OUT_LD * 4 <= RING, "staged partials reuse the TMA ring");
   static_assert(XT % 1024 == 0 && STAGE % 1024 == 0 && RAWT % 1024 == 0, "swizzle alignment");
-  static_assert(TMEM_COLS >= 32 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM allocation");
+  static_assert((WK == WK_I4 ? 2 : 1) * NT * ACC_COLS <= A_COL, "accumulator columns");
+  static_assert(A_COL + NA * NT * A_COLS <= TMEM_COLS, "operand columns");
   static constexpr size_t smem() { return 1024 + static_cast<size_t>(BYTES); }
 };
 
@@ -125,9 +133,9 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* full = bars;               // [NS] x tiles + raw weight tiles landed
   uint64_t* empty = full + NS;         // [NS] MMAs and converters done with the stage
-  uint64_t* aready = empty + NS;       // [NA] fp16 weights written
-  uint64_t* afree = aready + NA;       // [NA] MMAs done with them
-  uint64_t* acc_full = afree + NA;     // [2]
+  uint64_t* aready = empty + NS;       // [NA][NT] fp16 weights of a tile in TMEM
+  uint64_t* afree = aready + NA * NT;  // [NA][NT] the tile's MMAs done with them
+  uint64_t* acc_full = afree + NA * NT;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -141,18 +149,18 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
   auto xh_tile = [&](int s) { return smem + s * L::STAGE; };
   auto xl_tile = [&](int s) { return smem + s * L::STAGE + L::XT; };
   auto raw_tile = [&](int s, int j) { return smem + s * L::STAGE + 2 * L::XT + j * L::RAWT; };
-  auto a_tile = [&](int b, int j) { return smem + L::A_OFF + b * L::ABUF + j * A_TILE; };
+  auto a_col = [&](int b, int j) { return L::A_COL + static_cast<uint32_t>(b * NT + j) * L::A_COLS; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], NT + NT * 128);          // every tile's MMAs + the converters
+      mbar_init(&empty[s], 1 + NT * 128);           // the MMAs + the converters
     }
-    for (int b = 0; b < NA; ++b) {
-      mbar_init(&aready[b], NT * 128);
-      mbar_init(&afree[b], NT);
+    for (int b = 0; b < NA * NT; ++b) {
+      mbar_init(&aready[b], 128);
+      mbar_init(&afree[b], 1);
     }
-    for (int b = 0; b < 2; ++b) mbar_init(&acc_full[b], NT);
+    for (int b = 0; b < 2; ++b) mbar_init(&acc_full[b], 1);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&map_xh);
@@ -218,42 +226,53 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
       grid_dep_wait();
       grid_dep_launch();
     }
-  } else if (warp == 1 || warp >= kMmaWarpHi) {
-    // ---------------- MMA issue: one thread per weight tile ----------------
+  } else if (warp == 1) {
+    // ---------------- MMA issue: the whole warp, one elected lane ----------------
     grid_dep_wait();
     grid_dep_launch();
-    if (lane == 0) {
-      const int j = warp == 1 ? 0 : warp - kMmaWarpHi + 1;
-      constexpr uint32_t idesc = idesc_f16_f32(BW, 2 * MP);   // N: x hi rows, then lo rows
-      for (int i = 0; i < ntl && !*abort_flag; ++i) {
-        const int s = i % NS, b = i % NA;
-        const int gl = i / ktpg, buf = WK == WK_I4 ? (gl & 1) : 0;
-        const bool first = (i % ktpg) == 0;
-        // One wait per stage: an mbarrier wait in this thread stalls until
-        // the MMAs it has in flight complete (a few hundred cycles), so it
-        // waits on the converters' barrier alone.  The converters arrive there
-        // after observing this stage's TMA barrier (x tiles landed) and, in
-        // program order, after promoting the group whose TMEM buffer this
-        // stage's MMAs overwrite (fenced with tcgen05.fence::before_thread_sync).
-        if (!mbar_wait(&aready[b], (i / NA) & 1)) {
-          *abort_flag = 1;
-          break;
-        }
-        tc_fence_after();
-        // The lo tile follows the hi tile in shared memory, so one B operand
-        // of 2 * MP rows carries both terms: one MMA per K step.  A 32-byte
-        // step along K adds 2 to the descriptors' start-address field.
-        const uint64_t bdesc = desc_k_sw128(smem_u32(xh_tile(s)));
-        const uint64_t adesc = desc_k_sw128(smem_u32(a_tile(b, j)));
-        const uint32_t d = tmem + static_cast<uint32_t>((buf * NT + j) * 2 * MP);
-        mma_f16(d, adesc, bdesc, idesc, first ? 0u : 1u);
+    // INT4: N = MP, the hi- and lo-term MMAs into the same columns; INT8:
+    // N = 2 MP, the lo tile follows the hi tile in shared memory, so one B
+    // operand of 2 MP rows carries both terms into separate columns
+    constexpr uint32_t idesc = idesc_f16_f32(BW, WK == WK_I4 ? MP : 2 * MP);
+    for (int i = 0; i < ntl; ++i) {
+      const int s = i % NS, b = i % NA;
+      const int gl = i / ktpg, buf = WK == WK_I4 ? (gl & 1) : 0;
+      const bool first = (i % ktpg) == 0;
+      // Lane 0 waits for every tile's converters (they arrive after
+      // observing this stage's TMA barrier and, in program order, after
+      // promoting the group whose TMEM buffer this stage's MMAs overwrite,
+      // fenced with tcgen05.fence::before_thread_sync).
+      static_assert(NT == 2, "the ready test covers two tiles");
+      int got = 1;
+      if (lane == 0) {
+        const uint32_t ph = (i / NA) & 1;
+        got = mbar_test2(&aready[b * NT], ph, &aready[b * NT + 1], ph) ||
+              (!*abort_flag && mbar_wait(&aready[b * NT], ph) && mbar_wait(&aready[b * NT + 1], ph));
+        if (!got) *abort_flag = 1;
+      }
+      if (!__shfl_sync(0xffffffffu, got, 0)) break;
+      tc_fence_after();
+      if (elect_one()) {
+        // a 32-byte step along K adds 2 to the descriptor's start-address
+        // field and 8 columns to the TMEM operand address
+        const uint64_t bh = desc_k_sw128(smem_u32(xh_tile(s)));
+        const uint64_t bl = desc_k_sw128(smem_u32(xl_tile(s)));
 #pragma unroll
-        for (int kk = 1; kk < BK / 16; ++kk)
-          mma_f16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, 1u);
+        for (int j = 0; j < NT; ++j) {
+          const uint32_t at = tmem + a_col(b, j);
+          const uint32_t d = tmem + static_cast<uint32_t>(buf * NT + j) * L::ACC_COLS;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            mma_f16_ts(d, at + 8 * kk, bh + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
+            if (WK == WK_I4) mma_f16_ts(d, at + 8 * kk, bl + 2 * kk, idesc, 1u);
+          }
+        }
         mma_commit(&empty[s]);
-        mma_commit(&afree[b]);
+#pragma unroll
+        for (int j = 0; j < NT; ++j) mma_commit(&afree[b * NT + j]);
         if ((i % ktpg) == ktpg - 1 || i == ntl - 1) mma_commit(&acc_full[buf]);
       }
+      __syncwarp();
     }
   } else {
     // ---------------- converters + promotion (NT * 128 threads) ----------------
@@ -286,75 +305,107 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
       const int buf = WK == WK_I4 ? (gl & 1) : 0;
       const float sc = sc_next;
       if (WK == WK_I4 && gl + 1 < ngl) sc_next = group_scale(gl + 1);
-      if (!mbar_wait(&acc_full[buf], (gl >> 1) & 1)) return false;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (gl >> 1) & 1))) return false;
       tc_fence_after();
-      const uint32_t taddr = tmem + static_cast<uint32_t>((buf * NT + j) * 2 * MP) + (static_cast<uint32_t>(q * 32) << 16);
+      const uint32_t taddr = tmem + static_cast<uint32_t>(buf * NT + j) * L::ACC_COLS +
+                             (static_cast<uint32_t>(q * 32) << 16);
 #pragma unroll
       for (int c = 0; c < MP / 32; ++c) {
         float vh[32], vl[32];
         tmem_ld_32x32b_x32(taddr + c * 32, vh);
-        tmem_ld_32x32b_x32(taddr + MP + c * 32, vl);
+        if (WK == WK_I8) tmem_ld_32x32b_x32(taddr + MP + c * 32, vl);
         tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) acc[c * 32 + e] = fmaf(vh[e] + vl[e], sc, acc[c * 32 + e]);
+        for (int e = 0; e < 32; ++e)
+          acc[c * 32 + e] = fmaf(WK == WK_I8 ? vh[e] + vl[e] : vh[e], sc, acc[c * 32 + e]);
       }
       tc_fence_before();     // TMEM reads ordered before the next aready arrival
       return true;
     };
 
-    bool ok = true;
-    for (int i = 0; i < ntl && ok; ++i) {
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    // Software-pipelined: stage i + 1's barriers are tested and its raw
+    // words loaded while stage i's TMEM store is in flight.
+    constexpr int RW = WK == WK_I8 ? 4 : 2;         // 16-byte raw chunks per row and stage
+    uint4 rw[RW];
+    // stage i's TMA data landed and its operand buffer free (warp-uniform:
+    // the TMEM store and loads are .sync.aligned)
+    auto wait_stage = [&](int i) -> bool {
       const int s = i % NS, b = i % NA;
-      const int gl = i / ktpg;
-      if (*abort_flag || !mbar_wait(&full[s], (i / NS) & 1) ||
-          (i >= NA && !mbar_wait(&afree[b], ((i / NA) - 1) & 1))) {
-        ok = false;
-        break;
+      bool got;
+      if (i < NA) {
+        got = mbar_wait(&full[s], (i / NS) & 1);
+      } else {
+        const uint32_t pf = (i / NS) & 1, pa = ((i / NA) - 1) & 1;
+        got = mbar_test2(&full[s], pf, &afree[b * NT + j], pa) ||
+              (!*abort_flag && mbar_wait(&full[s], pf) && mbar_wait(&afree[b * NT + j], pa));
       }
-      // raw row -> fp16 row of the 128B-swizzled K-major operand
-      uint8_t* dst = a_tile(b, j) + (row >> 3) * 1024 + (row & 7) * 128;
-      const uint32_t rsw = static_cast<uint32_t>(row & 7);
+      return __all_sync(0xffffffffu, got);
+    };
+    auto load_raw = [&](int i) {
+      const int s = i % NS;
       if (WK == WK_I8) {
         const uint8_t* src = raw_tile(s, j) + row * BK;             // TMA 64B swizzle
         const uint32_t rs = static_cast<uint32_t>((row >> 1) & 3);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 w = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(c) ^ rs) << 4));
-          const uint32_t wx = w.x ^ 0x80808080u, wy = w.y ^ 0x80808080u, wz = w.z ^ 0x80808080u,
-                         ww = w.w ^ 0x80808080u;
-          uint4 o0, o1;
-          o0.x = i8pair_h2(wx, 0x5140u); o0.y = i8pair_h2(wx, 0x5342u);
-          o0.z = i8pair_h2(wy, 0x5140u); o0.w = i8pair_h2(wy, 0x5342u);
-          o1.x = i8pair_h2(wz, 0x5140u); o1.y = i8pair_h2(wz, 0x5342u);
-          o1.z = i8pair_h2(ww, 0x5140u); o1.w = i8pair_h2(ww, 0x5342u);
-          *reinterpret_cast<uint4*>(dst + (((2 * c) ^ rsw) << 4)) = o0;
-          *reinterpret_cast<uint4*>(dst + (((2 * c + 1) ^ rsw) << 4)) = o1;
-        }
+        for (int c = 0; c < RW; ++c)
+          rw[c] = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(c) ^ rs) << 4));
       } else {
         const uint8_t* src = raw_tile(s, j) + row * (BK / 2);       // TMA 32B swizzle
         const uint32_t rs = static_cast<uint32_t>((row >> 2) & 1);
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint4 w = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(c) ^ rs) << 4));
-          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        for (int c = 0; c < RW; ++c)
+          rw[c] = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(c) ^ rs) << 4));
+      }
+    };
+    bool ok = ntl == 0 || wait_stage(0);
+    if (ok && ntl > 0) load_raw(0);
+    for (int i = 0; i < ntl && ok; ++i) {
+      const int s = i % NS, b = i % NA;
+      const int gl = i / ktpg;
+      tc_fence_after();      // the MMAs that read this operand buffer have completed
+      // raw row -> 32 columns of fp16 pairs (this row's 64 K elements)
+      uint32_t h[32];
+      if (WK == WK_I8) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {        // one word = 8 elements = one 16-byte chunk
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t wx = rw[c].x ^ 0x80808080u, wy = rw[c].y ^ 0x80808080u,
+                         wz = rw[c].z ^ 0x80808080u, ww = rw[c].w ^ 0x80808080u;
+          h[8 * c + 0] = i8pair_h2(wx, 0x5140u); h[8 * c + 1] = i8pair_h2(wx, 0x5342u);
+          h[8 * c + 2] = i8pair_h2(wy, 0x5140u); h[8 * c + 3] = i8pair_h2(wy, 0x5342u);
+          h[8 * c + 4] = i8pair_h2(wz, 0x5140u); h[8 * c + 5] = i8pair_h2(wz, 0x5342u);
+          h[8 * c + 6] = i8pair_h2(ww, 0x5140u); h[8 * c + 7] = i8pair_h2(ww, 0x5342u);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t ws[4] = {rw[c].x, rw[c].y, rw[c].z, rw[c].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {        // one word = 8 elements = four columns
             const uint32_t lo = nib_lo(ws[e]), hi = nib_hi(ws[e]);
-            uint4 o;                           // element order [0,2,4,6,1,3,5,7]
-            o.x = i4pair_h2(lo, 0x5140u);
-            o.y = i4pair_h2(lo, 0x5342u);
-            o.z = i4pair_h2(hi, 0x5140u);
-            o.w = i4pair_h2(hi, 0x5342u);
-            *reinterpret_cast<uint4*>(dst + ((static_cast<uint32_t>(4 * c + e) ^ rsw) << 4)) = o;
+            const int o = 4 * (4 * c + e);     // element order [0,2,4,6,1,3,5,7]
+            h[o + 0] = i4pair_h2(lo, 0x5140u);
+            h[o + 1] = i4pair_h2(lo, 0x5342u);
+            h[o + 2] = i4pair_h2(hi, 0x5140u);
+            h[o + 3] = i4pair_h2(hi, 0x5342u);
           }
         }
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&aready[b]);
+      tmem_st_32x32b_x32(tmem + lane_base + a_col(b, j), h);
+      const bool next = i + 1 < ntl;
+      const bool next_ok = !next || wait_stage(i + 1);
+      if (next && next_ok) load_raw(i + 1);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&aready[b * NT + j]);
       mbar_arrive(&empty[s]);
+      if (!next_ok) {
+        ok = false;
+        break;
+      }
       if (WK == WK_I4 && (i % ktpg) == ktpg - 1 && gl >= 1 && !promote(gl - 1)) ok = false;
     }
-    if (ok && ntl > 0 && !*abort_flag) ok = promote(ngl - 1);
+    if (ok && ntl > 0 && __all_sync(0xffffffffu, !*abort_flag)) ok = promote(ngl - 1);
     if (!ok) {
       *abort_flag = 1;
       raise_flag(a.flags, KSH_FLAG_TIMEOUT);
@@ -467,9 +518,14 @@ struct MidPlan {
   int ctas, kt_total, kt_per_group, splits, kt_per_split;
 };
 
-// Split-K minimising (waves x K steps per CTA) at one CTA per SM, split
-// boundaries on group boundaries, at most kMaxSplits (one cluster).
-MidPlan mid_plan(int epi, int64_t keff, int64_t n_rows, int kt_per_group) {
+// Split-K minimising (waves x K steps per CTA) on the CTAs the GPU holds at
+// once in clusters of that split (slots_of(s)), split boundaries on group
+// boundaries, at most kMaxSplits (one cluster).  Counting the SMs alone
+// misjudged cluster placement: 16 clusters of 8 at one CTA per SM ran as two
+// waves (the down projection of the 8B shape at M = 64, SMs resident 47 % of
+// the kernel's time).
+template <typename SlotsFn>
+MidPlan mid_plan(int epi, int64_t keff, int64_t n_rows, int kt_per_group, SlotsFn slots_of) {
   MidPlan p = {};
   const int64_t rows_per_tile = epi == EPI_SWIGLU ? BW / 2 : BW;
   const int64_t out_rows = epi == EPI_SWIGLU ? n_rows / 2 : n_rows;
@@ -478,11 +534,11 @@ MidPlan mid_plan(int epi, int64_t keff, int64_t n_rows, int kt_per_group) {
   p.kt_total = static_cast<int>((keff + BK - 1) / BK);
   p.kt_per_group = kt_per_group;
   const int groups = (p.kt_total + kt_per_group - 1) / kt_per_group;
-  const int64_t slots = num_sms();
   double best = 1e30;
   for (int s = 1; s <= kMaxSplits && s <= groups; ++s) {
     const int kps = (groups + s - 1) / s * kt_per_group;
     if ((p.kt_total + kps - 1) / kps != s) continue;
+    const int64_t slots = std::max<int64_t>(s, slots_of(s));
     const int64_t waves = (static_cast<int64_t>(p.ctas) * s + slots - 1) / slots;
     const double cost = static_cast<double>(waves) * (kps + 3);
     if (cost < best - 1e-9) {
@@ -498,7 +554,13 @@ template <int WK, int EPI, int MP>
 int launch_mid(const LinArgs& a, char* ws, cudaStream_t stream) {
   using L = MidLayout<WK, MP>;
   const int64_t keff = WK == WK_I4 ? a.kp : a.k;
-  const MidPlan p = mid_plan(EPI, keff, a.n, WK == WK_I4 ? static_cast<int>(a.g / BK) : 1);
+  auto kern = qgemm_mid_kernel<WK, EPI, MP>;
+  if (set_smem_optin(reinterpret_cast<const void*>(kern), L::smem()) != KSH_OK) return KSH_ERR_CUDA;
+  const MidPlan p = mid_plan(EPI, keff, a.n, WK == WK_I4 ? static_cast<int>(a.g / BK) : 1,
+                             [&](int s) {
+                               return cluster_slots(reinterpret_cast<const void*>(kern), kThreads,
+                                                    L::smem(), s);
+                             });
   if (p.splits < 1) return KSH_ERR_UNSUPPORTED;
   __half *xh = nullptr, *xl = nullptr;
   float* inv = nullptr;
@@ -531,22 +593,25 @@ int launch_mid(const LinArgs& a, char* ws, cudaStream_t stream) {
   t.kt_per_split = p.kt_per_split;
   t.kt_per_group = p.kt_per_group;
   t.ngroups_row = WK == WK_I4 ? static_cast<int>(a.kp / a.g) : 1;
-  auto kern = qgemm_mid_kernel<WK, EPI, MP>;
-  if (set_smem_optin(reinterpret_cast<const void*>(kern), L::smem()) != KSH_OK) return KSH_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(p.ctas), static_cast<unsigned>(p.splits), 1);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = L::smem();
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;      // the splits of a CTA's tiles = one cluster
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = static_cast<unsigned>(p.splits);
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  int na = 0;
+  if (p.splits > 1) {                                     // the splits of a CTA's tiles = one cluster
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = static_cast<unsigned>(p.splits);
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[na].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  ++na;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = na;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mxh, mxl, mw, t);
   if (e == cudaSuccess) count_launch();
   return e == cudaSuccess ? KSH_OK : record_cuda_error(e);

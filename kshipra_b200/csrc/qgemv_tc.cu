@@ -1196,7 +1196,8 @@ struct GvPlan {
 };
 
 // Split-K that minimises (waves x K steps per CTA) on the resident CTA slots
-// (slots(kt_per_split): CTAs per GPU at that split's shared-memory size),
+// (slots(kt_per_split, split): CTAs the GPU holds at once at that split's
+// shared-memory size, in clusters of the split),
 // split boundaries on group boundaries, at most kMaxSplits (one cluster).
 template <typename SlotsFn>
 GvPlan gv_plan(int epi, int64_t keff, int64_t n_rows, int bk, int kt_per_group, SlotsFn slots_of) {
@@ -1213,7 +1214,7 @@ GvPlan gv_plan(int epi, int64_t keff, int64_t n_rows, int bk, int kt_per_group, 
     const int kps = gps * p.kt_per_group;
     const int real = (p.kt_total + kps - 1) / kps;
     if (real != s) continue;
-    const int64_t slots = slots_of(kps);
+    const int64_t slots = slots_of(kps, s);
     if (slots <= 0) continue;
     const int64_t ctas = static_cast<int64_t>(p.tiles) * s;
     const int64_t waves = (ctas + slots - 1) / slots;
@@ -1230,13 +1231,15 @@ GvPlan gv_plan(int epi, int64_t keff, int64_t n_rows, int bk, int kt_per_group, 
 
 constexpr size_t kMaxSmem = 227 * 1024;
 
-// CTAs of `kern` resident per SM at `smem` bytes: the smaller of the
-// occupancy query and the shared-memory bound (both CTAs' reservations).
-int64_t gv_slots(const void* kern, size_t smem, int threads = kThreads) {
+// CTAs of `kern` resident on the GPU at `smem` bytes in clusters of
+// `cluster`: the smaller of the occupancy query and the shared-memory bound
+// (both CTAs' reservations) per SM, and of the cluster-placement query.
+int64_t gv_slots(const void* kern, size_t smem, int cluster, int threads = kThreads) {
   if (smem > kMaxSmem) return 0;
   const int by_smem = static_cast<int>((228 * 1024) / (smem + 1024));
   const int occ = resident_ctas(kern, threads, smem);
-  return static_cast<int64_t>(num_sms()) * std::max(1, std::min(by_smem, std::max(occ, 1)));
+  const int64_t per_sm = static_cast<int64_t>(num_sms()) * std::max(1, std::min(by_smem, std::max(occ, 1)));
+  return cluster > 1 ? std::min(per_sm, cluster_slots(kern, threads, smem, cluster)) : per_sm;
 }
 
 GvArgs gv_args(const LinArgs& a, const GvPlan& p, int ngroups_row) {
@@ -1293,7 +1296,7 @@ int launch_gv(const LinArgs& a, cudaStream_t stream) {
   const int64_t keff = WK == WK_I4 ? a.kp : a.k;
   const int m = static_cast<int>(a.m);
   const GvPlan p = gv_plan(EPI, keff, a.n, BK, WK == WK_I4 ? static_cast<int>(a.g / BK) : 1,
-                           [&](int kps) { return gv_slots(kp, L::smem(m, kps)); });
+                           [&](int kps, int sp) { return gv_slots(kp, L::smem(m, kps), sp); });
   if (p.splits < 1) return KSH_ERR_UNSUPPORTED;
   CUtensorMap mw;
   const uint32_t box_rows = EPI == EPI_SWIGLU ? BW / 2 : BW;
@@ -1317,7 +1320,7 @@ int launch_gv_i8(const LinArgs& a, cudaStream_t stream) {
   if (set_smem_optin(kp, kMaxSmem) != KSH_OK) return KSH_ERR_CUDA;
   const int m = static_cast<int>(a.m);
   const GvPlan p = gv_plan(EPI, a.k, a.n, L::KS, 1,
-                           [&](int kps) { return gv_slots(kp, L::smem(m, kps)); });
+                           [&](int kps, int sp) { return gv_slots(kp, L::smem(m, kps), sp); });
   if (p.splits < 1) return KSH_ERR_UNSUPPORTED;
   CUtensorMap mw;
   const uint32_t box_rows = EPI == EPI_SWIGLU ? BW / 2 : BW;
@@ -1335,7 +1338,7 @@ int launch_gv_i4(const LinArgs& a, cudaStream_t stream) {
   const void* kp = reinterpret_cast<const void*>(kern);
   if (set_smem_optin(kp, kMaxSmem) != KSH_OK) return KSH_ERR_CUDA;
   const GvPlan p = gv_plan(EPI, a.kp, a.n, BK8, 1,
-                           [&](int kps) { return gv_slots(kp, L::smem(0, kps), kThreadsI4); });
+                           [&](int kps, int sp) { return gv_slots(kp, L::smem(0, kps), sp, kThreadsI4); });
   if (p.splits < 1) return KSH_ERR_UNSUPPORTED;
   CUtensorMap mw;
   const uint32_t box_rows = EPI == EPI_SWIGLU ? BW / 2 : BW;

@@ -3,6 +3,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <unordered_map>
@@ -172,6 +173,53 @@ __global__ void bounded_wait_check_kernel(uint32_t polls, int arrive,
   }
 }
 }  // namespace
+
+int64_t cluster_slots(const void* kernel, int threads, size_t smem, int cluster) {
+  if (cluster <= 1) return static_cast<int64_t>(resident_ctas(kernel, threads, smem)) * num_sms();
+  static std::mutex mu;
+  struct Key {
+    const void* k;
+    int dev, threads, cluster;
+    size_t smem;
+    bool operator==(const Key& o) const {
+      return k == o.k && dev == o.dev && threads == o.threads && cluster == o.cluster &&
+             smem == o.smem;
+    }
+  };
+  struct Hash {
+    size_t operator()(const Key& x) const {
+      return std::hash<const void*>()(x.k) ^ (static_cast<size_t>(x.dev) << 1) ^
+             (static_cast<size_t>(x.threads) << 8) ^ (static_cast<size_t>(x.cluster) << 16) ^
+             (x.smem << 24);
+    }
+  };
+  static std::unordered_map<Key, int64_t, Hash> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const Key key{kernel, dev, threads, cluster, smem};
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(cluster), 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = static_cast<unsigned>(cluster);
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = std::max(1, num_sms() / cluster);
+  }
+  const int64_t slots = static_cast<int64_t>(n) * cluster;
+  cache[key] = slots;
+  return slots;
+}
 
 }  // namespace ksh
 
