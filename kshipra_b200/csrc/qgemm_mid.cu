@@ -60,20 +60,27 @@ namespace {
 using namespace tc;
 
 constexpr int BW = 128;                 // weight rows per tile (MMA M)
-constexpr int BK = 64;                  // K per stage (one 128-byte fp16 row)
+constexpr int BK = 64;                  // K per sub-stage (one 128-byte fp16 row)
 constexpr int NT = 2;                   // weight tiles per CTA
-constexpr int NA = 4;                   // fp16 weight operand buffers (in TMEM)
 // warp 0: TMA; warp 1: MMAs of every tile (the whole warp converged, one
 // elected lane issuing); warps 2 .. 1 + 4 NT: converters
 constexpr int kConvWarp0 = 2;
 constexpr int kThreads = 32 * (kConvWarp0 + 4 * NT);
 constexpr int kMaxSplits = 8;
 
-template <int WK, int MP>
+// SK sub-stages of BK per pipeline stage: every barrier round trip (~200
+// cycles on a completed phase) and the per-stage bookkeeping of the MMA and
+// converter warps are paid once per SK * BK of K.
+template <int WK, int MP, int SK>
 struct MidLayout {
-  static constexpr int XT = MP * BK * 2;                      // one x term tile
-  static constexpr int RAWT = BW * (WK == WK_I8 ? BK : BK / 2);
-  static constexpr int STAGE = 2 * XT + NT * RAWT;
+  static constexpr int BKS = SK * BK;                         // K per stage
+  static constexpr int XT = MP * BK * 2;                      // one x term sub-tile
+  static constexpr int RAWT = BW * (WK == WK_I8 ? BK : BK / 2);  // one tile's raw sub-tile
+  // stage: [x hi k][x lo k] for every sub-stage k (the lo rows right after
+  // the hi rows: one INT8 B operand of 2 MP rows), then tile j's raw
+  // sub-tiles [j][k]
+  static constexpr int XSUB = 2 * XT;
+  static constexpr int STAGE = SK * XSUB + NT * SK * RAWT;
   static constexpr int NS = std::min(8, (200 * 1024) / STAGE);
   static constexpr int RING = NS * STAGE;
   static constexpr int BAR_OFF = RING;
@@ -83,12 +90,13 @@ struct MidLayout {
   // columns (the hi- and lo-term MMAs add into the same ones), two buffers
   // (one group promoted while the next accumulates); INT8 [hi: MP][lo: MP],
   // one buffer.  From A_COL the fp16 weight operands: per buffer and tile
-  // BK / 2 columns (two K-consecutive halves per column, one row per lane).
+  // BKS / 2 columns (two K-consecutive halves per column, one row per lane).
   static constexpr uint32_t ACC_COLS = WK == WK_I4 ? MP : 2 * MP;
   static constexpr uint32_t A_COL = 256;
-  static constexpr uint32_t A_COLS = BK / 2;
+  static constexpr uint32_t A_COLS = BKS / 2;
+  static constexpr int NA = static_cast<int>(256 / (NT * A_COLS));  // operand buffers
   static constexpr uint32_t TMEM_COLS = 512;
-  static_assert(NS >= 4, "pipeline depth");
+  static_assert(NS >= 3 && NA >= 2, "pipeline depth");
   static_assert(MP * OUT_LD * 4 <= RING, "staged partials reuse the TMA ring");
   static_assert(XT % 1024 == 0 && STAGE % 1024 == 0 && RAWT % 1024 == 0, "swizzle alignment");
   static_assert((WK == WK_I4 ? 2 : 1) * NT * ACC_COLS <= A_COL, "accumulator columns");
@@ -122,12 +130,12 @@ __device__ __forceinline__ uint32_t i4pair_h2(uint32_t nb, uint32_t sel) {
   return *reinterpret_cast<uint32_t*>(&r);
 }
 
-template <int WK, int EPI, int MP>
+template <int WK, int EPI, int MP, int SK>
 __global__ void __launch_bounds__(kThreads, 1)
 qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_constant__ CUtensorMap map_xl,
                  const __grid_constant__ CUtensorMap map_w, MidArgs a) {
-  using L = MidLayout<WK, MP>;
-  constexpr int NS = L::NS;
+  using L = MidLayout<WK, MP, SK>;
+  constexpr int NS = L::NS, NA = L::NA;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
@@ -146,18 +154,20 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
   const int ntl = max(kt_end - kt_begin, 0);
   const int ktpg = WK == WK_I4 ? a.kt_per_group : max(ntl, 1);
   const int ngl = (ntl + ktpg - 1) / ktpg;
-  auto xh_tile = [&](int s) { return smem + s * L::STAGE; };
-  auto xl_tile = [&](int s) { return smem + s * L::STAGE + L::XT; };
-  auto raw_tile = [&](int s, int j) { return smem + s * L::STAGE + 2 * L::XT + j * L::RAWT; };
+  auto xh_tile = [&](int s, int k) { return smem + s * L::STAGE + k * L::XSUB; };
+  auto xl_tile = [&](int s, int k) { return smem + s * L::STAGE + k * L::XSUB + L::XT; };
+  auto raw_tile = [&](int s, int j, int k) {
+    return smem + s * L::STAGE + SK * L::XSUB + (j * SK + k) * L::RAWT;
+  };
   auto a_col = [&](int b, int j) { return L::A_COL + static_cast<uint32_t>(b * NT + j) * L::A_COLS; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1 + NT * 128);           // the MMAs + the converters
+      mbar_init(&empty[s], 1 + NT * 4);             // the MMAs + every converter warp
     }
     for (int b = 0; b < NA * NT; ++b) {
-      mbar_init(&aready[b], 128);
+      mbar_init(&aready[b], 4);                     // the tile's four converter warps
       mbar_init(&afree[b], 1);
     }
     for (int b = 0; b < 2; ++b) mbar_init(&acc_full[b], 1);
@@ -183,24 +193,30 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
       auto issue_w = [&](int i) {
         const int s = i % NS;
         mbar_arrive_expect_tx(&full[s], L::STAGE);
-        const int kg = (kt_begin + i) * BK;
-        const int xw = WK == WK_I8 ? kg : kg / 2;
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          if (EPI == EPI_SWIGLU) {
-            const int r0 = (cta_tile + j) * (BW / 2);
-            tma_load_2d(raw_tile(s, j), &map_w, &full[s], xw, r0);
-            tma_load_2d(raw_tile(s, j) + L::RAWT / 2, &map_w, &full[s], xw, a.inter + r0);
-          } else {
-            tma_load_2d(raw_tile(s, j), &map_w, &full[s], xw, (cta_tile + j) * BW);
+        for (int k = 0; k < SK; ++k) {
+          const int kg = (kt_begin + i) * L::BKS + k * BK;
+          const int xw = WK == WK_I8 ? kg : kg / 2;
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            if (EPI == EPI_SWIGLU) {
+              const int r0 = (cta_tile + j) * (BW / 2);
+              tma_load_2d(raw_tile(s, j, k), &map_w, &full[s], xw, r0);
+              tma_load_2d(raw_tile(s, j, k) + L::RAWT / 2, &map_w, &full[s], xw, a.inter + r0);
+            } else {
+              tma_load_2d(raw_tile(s, j, k), &map_w, &full[s], xw, (cta_tile + j) * BW);
+            }
           }
         }
       };
       auto issue_x = [&](int i) {
         const int s = i % NS;
-        const int kg = (kt_begin + i) * BK;
-        tma_load_2d(xh_tile(s), &map_xh, &full[s], kg, 0);
-        tma_load_2d(xl_tile(s), &map_xl, &full[s], kg, 0);
+#pragma unroll
+        for (int k = 0; k < SK; ++k) {
+          const int kg = (kt_begin + i) * L::BKS + k * BK;
+          tma_load_2d(xh_tile(s, k), &map_xh, &full[s], kg, 0);
+          tma_load_2d(xl_tile(s, k), &map_xl, &full[s], kg, 0);
+        }
       };
       // weights are constant: their first stages go out before the dependency
       // wait; x is written by the preceding split kernel
@@ -234,43 +250,48 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
     // N = 2 MP, the lo tile follows the hi tile in shared memory, so one B
     // operand of 2 MP rows carries both terms into separate columns
     constexpr uint32_t idesc = idesc_f16_f32(BW, WK == WK_I4 ? MP : 2 * MP);
-    for (int i = 0; i < ntl; ++i) {
+    // group and position in it, counted (no division by the runtime group length)
+    int gl = 0, kin = 0;
+    for (int i = 0; i < ntl; ++i, (++kin == ktpg) ? (kin = 0, ++gl) : 0) {
       const int s = i % NS, b = i % NA;
-      const int gl = i / ktpg, buf = WK == WK_I4 ? (gl & 1) : 0;
-      const bool first = (i % ktpg) == 0;
-      // Lane 0 waits for every tile's converters (they arrive after
+      const int buf = WK == WK_I4 ? (gl & 1) : 0;
+      const bool first = kin == 0;
+      // Lane 1 waits for every tile's converters (they arrive after
       // observing this stage's TMA barrier and, in program order, after
       // promoting the group whose TMEM buffer this stage's MMAs overwrite,
       // fenced with tcgen05.fence::before_thread_sync).
       static_assert(NT == 2, "the ready test covers two tiles");
       int got = 1;
-      if (lane == 0) {
+      if (lane == 1) {
         const uint32_t ph = (i / NA) & 1;
         got = mbar_test2(&aready[b * NT], ph, &aready[b * NT + 1], ph) ||
               (!*abort_flag && mbar_wait(&aready[b * NT], ph) && mbar_wait(&aready[b * NT + 1], ph));
         if (!got) *abort_flag = 1;
       }
-      if (!__shfl_sync(0xffffffffu, got, 0)) break;
+      if (!__shfl_sync(0xffffffffu, got, 1)) break;
       tc_fence_after();
       if (elect_one()) {
         // a 32-byte step along K adds 2 to the descriptor's start-address
         // field and 8 columns to the TMEM operand address
-        const uint64_t bh = desc_k_sw128(smem_u32(xh_tile(s)));
-        const uint64_t bl = desc_k_sw128(smem_u32(xl_tile(s)));
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          const uint32_t at = tmem + a_col(b, j);
-          const uint32_t d = tmem + static_cast<uint32_t>(buf * NT + j) * L::ACC_COLS;
+        for (int k = 0; k < SK; ++k) {
+          const uint64_t bh = desc_k_sw128(smem_u32(xh_tile(s, k)));
+          const uint64_t bl = desc_k_sw128(smem_u32(xl_tile(s, k)));
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            mma_f16_ts(d, at + 8 * kk, bh + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
-            if (WK == WK_I4) mma_f16_ts(d, at + 8 * kk, bl + 2 * kk, idesc, 1u);
+          for (int j = 0; j < NT; ++j) {
+            const uint32_t at = tmem + a_col(b, j) + static_cast<uint32_t>(k * (BK / 2));
+            const uint32_t d = tmem + static_cast<uint32_t>(buf * NT + j) * L::ACC_COLS;
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              mma_f16_ts(d, at + 8 * kk, bh + 2 * kk, idesc, (first && k == 0 && kk == 0) ? 0u : 1u);
+              if (WK == WK_I4) mma_f16_ts(d, at + 8 * kk, bl + 2 * kk, idesc, 1u);
+            }
           }
         }
         mma_commit(&empty[s]);
 #pragma unroll
         for (int j = 0; j < NT; ++j) mma_commit(&afree[b * NT + j]);
-        if ((i % ktpg) == ktpg - 1 || i == ntl - 1) mma_commit(&acc_full[buf]);
+        if (kin == ktpg - 1 || i == ntl - 1) mma_commit(&acc_full[buf]);
       }
       __syncwarp();
     }
@@ -294,7 +315,7 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
     auto group_scale = [&](int gl) -> float {
       if (wrow < 0) return 0.0f;
       if (WK == WK_I8) return __half2float(a.scales[wrow]);
-      return __half2float(a.scales[static_cast<int64_t>(wrow) * a.ngroups_row + (kt_begin + gl * ktpg) / ktpg]);
+      return __half2float(a.scales[static_cast<int64_t>(wrow) * a.ngroups_row + kt_begin / ktpg + gl]);
     };
     float acc[MP];
 #pragma unroll
@@ -326,8 +347,8 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     // Software-pipelined: stage i + 1's barriers are tested and its raw
     // words loaded while stage i's TMEM store is in flight.
-    constexpr int RW = WK == WK_I8 ? 4 : 2;         // 16-byte raw chunks per row and stage
-    uint4 rw[RW];
+    constexpr int RW = WK == WK_I8 ? 4 : 2;         // 16-byte raw chunks per row and sub-stage
+    uint4 rw[SK][RW];
     // stage i's TMA data landed and its operand buffer free (warp-uniform:
     // the TMEM store and loads are .sync.aligned)
     auto wait_stage = [&](int i) -> bool {
@@ -344,66 +365,76 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
     };
     auto load_raw = [&](int i) {
       const int s = i % NS;
-      if (WK == WK_I8) {
-        const uint8_t* src = raw_tile(s, j) + row * BK;             // TMA 64B swizzle
-        const uint32_t rs = static_cast<uint32_t>((row >> 1) & 3);
 #pragma unroll
-        for (int c = 0; c < RW; ++c)
-          rw[c] = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(c) ^ rs) << 4));
-      } else {
-        const uint8_t* src = raw_tile(s, j) + row * (BK / 2);       // TMA 32B swizzle
-        const uint32_t rs = static_cast<uint32_t>((row >> 2) & 1);
+      for (int k = 0; k < SK; ++k) {
+        if (WK == WK_I8) {
+          const uint8_t* src = raw_tile(s, j, k) + row * BK;        // TMA 64B swizzle
+          const uint32_t rs = static_cast<uint32_t>((row >> 1) & 3);
 #pragma unroll
-        for (int c = 0; c < RW; ++c)
-          rw[c] = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(c) ^ rs) << 4));
+          for (int c = 0; c < RW; ++c)
+            rw[k][c] = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(c) ^ rs) << 4));
+        } else {
+          const uint8_t* src = raw_tile(s, j, k) + row * (BK / 2);  // TMA 32B swizzle
+          const uint32_t rs = static_cast<uint32_t>((row >> 2) & 1);
+#pragma unroll
+          for (int c = 0; c < RW; ++c)
+            rw[k][c] = *reinterpret_cast<const uint4*>(src + ((static_cast<uint32_t>(c) ^ rs) << 4));
+        }
       }
     };
     bool ok = ntl == 0 || wait_stage(0);
     if (ok && ntl > 0) load_raw(0);
-    for (int i = 0; i < ntl && ok; ++i) {
+    int gl = 0, kin = 0;
+    for (int i = 0; i < ntl && ok; ++i, (++kin == ktpg) ? (kin = 0, ++gl) : 0) {
       const int s = i % NS, b = i % NA;
-      const int gl = i / ktpg;
       tc_fence_after();      // the MMAs that read this operand buffer have completed
-      // raw row -> 32 columns of fp16 pairs (this row's 64 K elements)
-      uint32_t h[32];
-      if (WK == WK_I8) {
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint32_t wx = rw[c].x ^ 0x80808080u, wy = rw[c].y ^ 0x80808080u,
-                         wz = rw[c].z ^ 0x80808080u, ww = rw[c].w ^ 0x80808080u;
-          h[8 * c + 0] = i8pair_h2(wx, 0x5140u); h[8 * c + 1] = i8pair_h2(wx, 0x5342u);
-          h[8 * c + 2] = i8pair_h2(wy, 0x5140u); h[8 * c + 3] = i8pair_h2(wy, 0x5342u);
-          h[8 * c + 4] = i8pair_h2(wz, 0x5140u); h[8 * c + 5] = i8pair_h2(wz, 0x5342u);
-          h[8 * c + 6] = i8pair_h2(ww, 0x5140u); h[8 * c + 7] = i8pair_h2(ww, 0x5342u);
-        }
-      } else {
+      for (int k = 0; k < SK; ++k) {
+        // raw row -> 32 columns of fp16 pairs (this row's 64 K elements of sub-stage k)
+        uint32_t h[32];
+        if (WK == WK_I8) {
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const uint32_t ws[4] = {rw[c].x, rw[c].y, rw[c].z, rw[c].w};
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t wx = rw[k][c].x ^ 0x80808080u, wy = rw[k][c].y ^ 0x80808080u,
+                           wz = rw[k][c].z ^ 0x80808080u, ww = rw[k][c].w ^ 0x80808080u;
+            h[8 * c + 0] = i8pair_h2(wx, 0x5140u); h[8 * c + 1] = i8pair_h2(wx, 0x5342u);
+            h[8 * c + 2] = i8pair_h2(wy, 0x5140u); h[8 * c + 3] = i8pair_h2(wy, 0x5342u);
+            h[8 * c + 4] = i8pair_h2(wz, 0x5140u); h[8 * c + 5] = i8pair_h2(wz, 0x5342u);
+            h[8 * c + 6] = i8pair_h2(ww, 0x5140u); h[8 * c + 7] = i8pair_h2(ww, 0x5342u);
+          }
+        } else {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {        // one word = 8 elements = four columns
-            const uint32_t lo = nib_lo(ws[e]), hi = nib_hi(ws[e]);
-            const int o = 4 * (4 * c + e);     // element order [0,2,4,6,1,3,5,7]
-            h[o + 0] = i4pair_h2(lo, 0x5140u);
-            h[o + 1] = i4pair_h2(lo, 0x5342u);
-            h[o + 2] = i4pair_h2(hi, 0x5140u);
-            h[o + 3] = i4pair_h2(hi, 0x5342u);
+          for (int c = 0; c < 2; ++c) {
+            const uint32_t ws[4] = {rw[k][c].x, rw[k][c].y, rw[k][c].z, rw[k][c].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {      // one word = 8 elements = four columns
+              const uint32_t lo = nib_lo(ws[e]), hi = nib_hi(ws[e]);
+              const int o = 4 * (4 * c + e);   // element order [0,2,4,6,1,3,5,7]
+              h[o + 0] = i4pair_h2(lo, 0x5140u);
+              h[o + 1] = i4pair_h2(lo, 0x5342u);
+              h[o + 2] = i4pair_h2(hi, 0x5140u);
+              h[o + 3] = i4pair_h2(hi, 0x5342u);
+            }
           }
         }
+        tmem_st_32x32b_x32(tmem + lane_base + a_col(b, j) + static_cast<uint32_t>(k * (BK / 2)), h);
       }
-      tmem_st_32x32b_x32(tmem + lane_base + a_col(b, j), h);
       const bool next = i + 1 < ntl;
       const bool next_ok = !next || wait_stage(i + 1);
       if (next && next_ok) load_raw(i + 1);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&aready[b * NT + j]);
-      mbar_arrive(&empty[s]);
+      // one arrival per warp (the barriers count warps)
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&aready[b * NT + j]);
+        mbar_arrive(&empty[s]);
+      }
       if (!next_ok) {
         ok = false;
         break;
       }
-      if (WK == WK_I4 && (i % ktpg) == ktpg - 1 && gl >= 1 && !promote(gl - 1)) ok = false;
+      if (WK == WK_I4 && kin == ktpg - 1 && gl >= 1 && !promote(gl - 1)) ok = false;
     }
     if (ok && ntl > 0 && __all_sync(0xffffffffu, !*abort_flag)) ok = promote(ngl - 1);
     if (!ok) {
@@ -525,13 +556,13 @@ struct MidPlan {
 // waves (the down projection of the 8B shape at M = 64, SMs resident 47 % of
 // the kernel's time).
 template <typename SlotsFn>
-MidPlan mid_plan(int epi, int64_t keff, int64_t n_rows, int kt_per_group, SlotsFn slots_of) {
+MidPlan mid_plan(int epi, int64_t keff, int64_t n_rows, int bks, int kt_per_group, SlotsFn slots_of) {
   MidPlan p = {};
   const int64_t rows_per_tile = epi == EPI_SWIGLU ? BW / 2 : BW;
   const int64_t out_rows = epi == EPI_SWIGLU ? n_rows / 2 : n_rows;
   const int64_t tiles = (out_rows + rows_per_tile - 1) / rows_per_tile;
   p.ctas = static_cast<int>((tiles + NT - 1) / NT);
-  p.kt_total = static_cast<int>((keff + BK - 1) / BK);
+  p.kt_total = static_cast<int>((keff + bks - 1) / bks);
   p.kt_per_group = kt_per_group;
   const int groups = (p.kt_total + kt_per_group - 1) / kt_per_group;
   double best = 1e30;
@@ -540,7 +571,7 @@ MidPlan mid_plan(int epi, int64_t keff, int64_t n_rows, int kt_per_group, SlotsF
     if ((p.kt_total + kps - 1) / kps != s) continue;
     const int64_t slots = std::max<int64_t>(s, slots_of(s));
     const int64_t waves = (static_cast<int64_t>(p.ctas) * s + slots - 1) / slots;
-    const double cost = static_cast<double>(waves) * (kps + 3);
+    const double cost = static_cast<double>(waves) * (kps * (bks / BK) + 3);   // in BK steps
     if (cost < best - 1e-9) {
       best = cost;
       p.splits = s;
@@ -550,13 +581,13 @@ MidPlan mid_plan(int epi, int64_t keff, int64_t n_rows, int kt_per_group, SlotsF
   return p;
 }
 
-template <int WK, int EPI, int MP>
+template <int WK, int EPI, int MP, int SK>
 int launch_mid(const LinArgs& a, char* ws, cudaStream_t stream) {
-  using L = MidLayout<WK, MP>;
+  using L = MidLayout<WK, MP, SK>;
   const int64_t keff = WK == WK_I4 ? a.kp : a.k;
-  auto kern = qgemm_mid_kernel<WK, EPI, MP>;
+  auto kern = qgemm_mid_kernel<WK, EPI, MP, SK>;
   if (set_smem_optin(reinterpret_cast<const void*>(kern), L::smem()) != KSH_OK) return KSH_ERR_CUDA;
-  const MidPlan p = mid_plan(EPI, keff, a.n, WK == WK_I4 ? static_cast<int>(a.g / BK) : 1,
+  const MidPlan p = mid_plan(EPI, keff, a.n, L::BKS, WK == WK_I4 ? static_cast<int>(a.g / L::BKS) : 1,
                              [&](int s) {
                                return cluster_slots(reinterpret_cast<const void*>(kern), kThreads,
                                                     L::smem(), s);
@@ -617,10 +648,17 @@ int launch_mid(const LinArgs& a, char* ws, cudaStream_t stream) {
   return e == cudaSuccess ? KSH_OK : record_cuda_error(e);
 }
 
+// INT4 with groups of whole 128-wide stages: two sub-stages per stage (the
+// promotion once per stage).  INT8 keeps 64-wide stages: its 64 KB stages of
+// two sub-stages leave room for three in the ring, too shallow to cover the
+// weight stream (40.7 -> 46.8 us at 4096 x 28672, M = 64).
 template <int WK, int EPI>
 int launch_mid_m(const LinArgs& a, char* ws, cudaStream_t stream) {
-  if (a.m <= 32) return launch_mid<WK, EPI, 32>(a, ws, stream);
-  return launch_mid<WK, EPI, 64>(a, ws, stream);
+  if constexpr (WK == WK_I4) {
+    if (a.g % (2 * BK) == 0)
+      return a.m <= 32 ? launch_mid<WK, EPI, 32, 2>(a, ws, stream) : launch_mid<WK, EPI, 64, 2>(a, ws, stream);
+  }
+  return a.m <= 32 ? launch_mid<WK, EPI, 32, 1>(a, ws, stream) : launch_mid<WK, EPI, 64, 1>(a, ws, stream);
 }
 
 }  // namespace
