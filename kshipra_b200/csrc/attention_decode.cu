@@ -18,7 +18,7 @@
 // * after the wait all warps rotate the g query heads of the group; the CTA
 //   holding the last tile also rotates k and writes k and v to the pool (for
 //   later steps);
-// * consumer warps 1..3 take whole tiles round-robin, each with its own
+// * consumer warps 1..2 take whole tiles round-robin, each with its own
 //   online-softmax state: scores (q . k) / sqrt(D) with the causal bound, the
 //   reference's merge (running max with m_safe, exp, rescale) and P.V.  A
 //   tile needs no CTA-wide barrier, so tiles of different warps overlap; the
@@ -45,10 +45,13 @@ namespace {
 using namespace tc;
 
 constexpr int kTK = 16;                          // keys per tile
-constexpr int kConsumers = 3;                    // consumer warps per CTA
+constexpr int kConsumers = 2;                    // consumer warps per CTA
 constexpr int kThreads = 32 * (kConsumers + 1);  // + the TMA producer warp
 constexpr int kMaxCluster = 8;
-constexpr int kRingBytes = 96 * 1024;            // two CTAs per SM
+// three CTAs per SM: 2 consumers and a 64 KB ring per CTA streamed 0.90 of
+// measured HBM at the Llama-3-8B shape, 3 consumers and 96 KB (two CTAs per
+// SM) 0.83, 2 consumers and 96 KB 0.71
+constexpr int kRingBytes = 64 * 1024;
 
 // 0: cluster size chosen per launch; KSH_DECODE_SPLIT=1..8 in the environment forces it
 int g_forced_split = [] {
@@ -87,7 +90,7 @@ struct DecLayout {
   static constexpr int D4 = D / 4;
   static constexpr int TILE_F = kTK * D;                 // floats per K (or V) tile
   static constexpr int STAGE_F = 2 * TILE_F;             // K tile then V tile
-  // 6 stages (D 128) / 12 (D 64), a multiple of the consumer count: tile i
+  // 4 stages (D 128) / 8 (D 64), a multiple of the consumer count: tile i
   // sits in stage i % NST and belongs to consumer i % kConsumers, so each
   // stage is only ever read by one consumer, which waits on it again only
   // after releasing it -- its full barrier is never more than one phase
@@ -118,7 +121,7 @@ struct DecLayout {
 // output.  Any split count then fills the SMs' resident slots, which a
 // cluster split, tied to cluster placement, does not.
 template <int D, int G, bool GS>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 3)
 decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
   using Ly = DecLayout<D, G>;
   constexpr int D4 = Ly::D4, TILE_F = Ly::TILE_F, STAGE_F = Ly::STAGE_F, NST = Ly::NST;
