@@ -128,6 +128,9 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
   constexpr int QS = Ly::QS, GP = Ly::GP;
   constexpr int GH = (G + 1) / 2;        // heads per lane in the score phase
   constexpr int NACC = GH == 1 ? 4 : (GH == 2 ? 2 : 1);  // independent partial sums per head
+  // D 128 with 4 heads per group (the Llama-3-8B shape): lanes split D instead
+  // of keys for q.k (see the consumer loop)
+  constexpr bool kBfly = D == 128 && G == 4;
   extern __shared__ __align__(128) float4 sm4[];
   // TMA 128B-swizzled destinations need 1024-byte alignment
   float* sm = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(sm4) + 1023) & ~uintptr_t(1023));
@@ -274,6 +277,11 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
     const int r = lane & (kTK - 1), hg = lane >> 4;
     float* P = Ps + cw * Ly::PW;
     bool bad = false;
+    float4 qf[kBfly ? G : 1];                    // this lane's 4-float column of every head's q
+    if constexpr (kBfly) {
+#pragma unroll
+      for (int h = 0; h < G; ++h) qf[h] = *reinterpret_cast<const float4*>(Qs + h * QS + 4 * lane);
+    }
     for (int i = cw; i < ntl; i += kConsumers) {
       const int s = i % NST;
       const bool arrived = mbar_wait(&full[s], (i / NST) & 1);
@@ -293,52 +301,99 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
         }
         __syncwarp();
       }
-      const bool valid = ok && (t_begin + i) * kTK + r < total_c;
-      // scores: lane -> key r, heads hg, hg + 2, ...
-      float dot[GH][NACC];
+      if constexpr (kBfly) {
+        // scores: lane -> 4-float column slice of D for all 16 keys x 4 heads
+        // (q in registers, one conflict-free K row read per key); the 64
+        // partial dot products are summed over the warp by a reduce-scatter
+        // butterfly (round m keeps the half of the values that lane bit m
+        // selects) that leaves lane l head l >> 3 at keys 2 (l & 7) + {0, 1}
+        float v[4 * kTK];
 #pragma unroll
-      for (int u = 0; u < GH; ++u)
+        for (int rr = 0; rr < kTK; ++rr) {
+          const float4 kv = *reinterpret_cast<const float4*>(Kt + tile_off<D>(rr, lane));
 #pragma unroll
-        for (int e = 0; e < NACC; ++e) dot[u][e] = 0.0f;
+          for (int h = 0; h < 4; ++h)
+            v[h * kTK + rr] = fmaf(qf[h].x, kv.x, fmaf(qf[h].y, kv.y, fmaf(qf[h].z, kv.z, qf[h].w * kv.w)));
+        }
 #pragma unroll
-      for (int d4 = 0; d4 < D4; ++d4) {
-        const float4 kv = *reinterpret_cast<const float4*>(Kt + tile_off<D>(r, d4));
+        for (int rd = 0; rd < 5; ++rd) {
+          const int m = 16 >> rd, half = 32 >> rd;
+          const bool upper = (lane & m) != 0;
+#pragma unroll
+          for (int j = 0; j < half; ++j) {
+            const float keep = upper ? v[j + half] : v[j];
+            const float send = upper ? v[j] : v[j + half];
+            v[j] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+          }
+        }
+        // online softmax of head hh over the tile's keys (8 lanes x 2 keys)
+        const int hh = lane >> 3, r0 = 2 * (lane & 7);
+        const int kb = (t_begin + i) * kTK;
+        const float s0 = (ok && kb + r0 < total_c) ? v[0] * a.scale : -INFINITY;
+        const float s1 = (ok && kb + r0 + 1 < total_c) ? v[1] * a.scale : -INFINITY;
+        float tmax = fmaxf(s0, s1);
+#pragma unroll
+        for (int o = 4; o >= 1; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+        const float m_new = fmaxf(m_run[0], tmax);
+        const float m_safe = isinf(m_new) ? 0.0f : m_new;
+        const float p0 = expf(s0 - m_safe), p1 = expf(s1 - m_safe);
+        float psum = p0 + p1;
+#pragma unroll
+        for (int o = 4; o >= 1; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+        const float corr = expf(m_run[0] - m_safe);
+        l_run[0] = __fadd_rn(__fmul_rn(l_run[0], corr), psum);
+        m_run[0] = m_new;
+        P[r0 * GP + hh] = p0;
+        P[(r0 + 1) * GP + hh] = p1;
+        if ((lane & 7) == 0) P[kTK * GP + hh] = corr;
+      } else {
+        const bool valid = ok && (t_begin + i) * kTK + r < total_c;
+        // scores: lane -> key r, heads hg, hg + 2, ...
+        float dot[GH][NACC];
+#pragma unroll
+        for (int u = 0; u < GH; ++u)
+#pragma unroll
+          for (int e = 0; e < NACC; ++e) dot[u][e] = 0.0f;
+#pragma unroll
+        for (int d4 = 0; d4 < D4; ++d4) {
+          const float4 kv = *reinterpret_cast<const float4*>(Kt + tile_off<D>(r, d4));
+#pragma unroll
+          for (int u = 0; u < GH; ++u) {
+            const int h = hg + 2 * u;
+            if (G % 2 == 0 || h < G) {
+              const float4 qv = *reinterpret_cast<const float4*>(Qs + h * QS + 4 * d4);
+              float& dd = dot[u][d4 % NACC];
+              dd = fmaf(qv.x, kv.x, dd);
+              dd = fmaf(qv.y, kv.y, dd);
+              dd = fmaf(qv.z, kv.z, dd);
+              dd = fmaf(qv.w, kv.w, dd);
+            }
+          }
+        }
+        // online softmax over the tile's 16 keys (the lanes of one half-warp)
 #pragma unroll
         for (int u = 0; u < GH; ++u) {
           const int h = hg + 2 * u;
-          if (G % 2 == 0 || h < G) {
-            const float4 qv = *reinterpret_cast<const float4*>(Qs + h * QS + 4 * d4);
-            float& dd = dot[u][d4 % NACC];
-            dd = fmaf(qv.x, kv.x, dd);
-            dd = fmaf(qv.y, kv.y, dd);
-            dd = fmaf(qv.z, kv.z, dd);
-            dd = fmaf(qv.w, kv.w, dd);
+          float sc = dot[u][0];
+#pragma unroll
+          for (int e = 1; e < NACC; ++e) sc += dot[u][e];
+          const float sv = (valid && h < G) ? sc * a.scale : -INFINITY;
+          float tmax = sv;
+#pragma unroll
+          for (int o = 8; o >= 1; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+          const float m_new = fmaxf(m_run[u], tmax);
+          const float m_safe = isinf(m_new) ? 0.0f : m_new;
+          const float pj = expf(sv - m_safe);
+          float psum = pj;
+#pragma unroll
+          for (int o = 8; o >= 1; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+          const float corr = expf(m_run[u] - m_safe);
+          l_run[u] = __fadd_rn(__fmul_rn(l_run[u], corr), psum);
+          m_run[u] = m_new;
+          if (h < G) {
+            P[r * GP + h] = pj;
+            if (r == 0) P[kTK * GP + h] = corr;
           }
-        }
-      }
-      // online softmax over the tile's 16 keys (the lanes of one half-warp)
-#pragma unroll
-      for (int u = 0; u < GH; ++u) {
-        const int h = hg + 2 * u;
-        float sc = dot[u][0];
-#pragma unroll
-        for (int e = 1; e < NACC; ++e) sc += dot[u][e];
-        const float sv = (valid && h < G) ? sc * a.scale : -INFINITY;
-        float tmax = sv;
-#pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
-        const float m_new = fmaxf(m_run[u], tmax);
-        const float m_safe = isinf(m_new) ? 0.0f : m_new;
-        const float pj = expf(sv - m_safe);
-        float psum = pj;
-#pragma unroll
-        for (int o = 8; o >= 1; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
-        const float corr = expf(m_run[u] - m_safe);
-        l_run[u] = __fadd_rn(__fmul_rn(l_run[u], corr), psum);
-        m_run[u] = m_new;
-        if (h < G) {
-          P[r * GP + h] = pj;
-          if (r == 0) P[kTK * GP + h] = corr;
         }
       }
       __syncwarp();
@@ -407,7 +462,12 @@ decode_attn_kernel(const __grid_constant__ CUtensorMap pool_map, DecArgs a) {
       for (int h = 0; h < G; ++h)
         reinterpret_cast<float4*>(wst + (cw * G + h) * (D + 4) + 4)[lane] = acc[h];
     }
-    if (r == 0) {
+    if constexpr (kBfly) {
+      if ((lane & 7) == 0) {                     // lane l ran head l >> 3
+        wst[(cw * G + (lane >> 3)) * (D + 4)] = m_run[0];
+        wst[(cw * G + (lane >> 3)) * (D + 4) + 1] = l_run[0];
+      }
+    } else if (r == 0) {
 #pragma unroll
       for (int u = 0; u < GH; ++u) {
         const int h = hg + 2 * u;
