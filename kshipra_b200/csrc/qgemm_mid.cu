@@ -264,8 +264,16 @@ qgemm_mid_kernel(const __grid_constant__ CUtensorMap map_xh, const __grid_consta
       int got = 1;
       if (lane == 1) {
         const uint32_t ph = (i / NA) & 1;
-        got = mbar_test2(&aready[b * NT], ph, &aready[b * NT + 1], ph) ||
-              (!*abort_flag && mbar_wait(&aready[b * NT], ph) && mbar_wait(&aready[b * NT + 1], ph));
+        // a non-blocking test in a bounded loop: a blocking try_wait may
+        // suspend the thread past the converters' arrival
+        got = 0;
+        for (uint32_t it = 0; it < (1u << 22); ++it) {
+          if (mbar_test2(&aready[b * NT], ph, &aready[b * NT + 1], ph)) {
+            got = 1;
+            break;
+          }
+          if ((it & 1023u) == 1023u && *abort_flag) break;
+        }
         if (!got) *abort_flag = 1;
       }
       if (!__shfl_sync(0xffffffffu, got, 1)) break;
